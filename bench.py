@@ -1,0 +1,415 @@
+#!/usr/bin/env python3
+"""Headline benchmark: the sm_100a BF16 GEMM on BASELINE config 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+
+Workload: C = A * B^T with A (M x K) and B (N x K)
+BF16 from N(0,1) (torch.Generator seed 0), FP32 accumulation, BF16 C, M = N =
+K = 4096 per GPU. At N GPUs the global problem is (4096 N) x 4096 x 4096 with
+A and C row-sharded (rank r owns rows [4096 r, 4096 (r+1))) and B replicated:
+per-GPU work is fixed ("weak" scaling) and no collective runs on the data
+path. One step = one GEMM launch over the rank's shard.
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
+on the GEMM's stream; L2 is flushed (a 256 MiB write) before every step,
+outside the events. A barrier + synchronize bracket the timed region, and
+the per-step time is the max over ranks. ``e2e`` times the same step through
+the C ABI with host buffers (bb_gemm_run_host: H2D A-shard and B from pinned
+memory, GEMM, D2H C).
+
+``--impl reference`` times the reference's CPU implementation of the path,
+the FP32 matmul oracle of gemm_comparison.py:2698-2715 (torch on the host
+cores, all threads), on row samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M_PER_RANK = 4096
+N_DIM = 4096
+K_DIM = 4096
+FLUSH_BYTES = 256 << 20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on BASELINE config 0 (4096^3 per GPU)")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--variant", default="tuned")
+    ap.add_argument("--no-cublaslt", action="store_true", help="skip the cuBLASLt comparator leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.steps < 1:
+        ap.error("--steps must be >= 1")
+    return args
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per launch of the GEMM from the committed ncu summary."""
+    path = ROOT / "profiles" / "gemm_tuned_4096_traffic.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["dram_bytes_per_launch"])
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def all_max(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_matmul_sample(target_s: float = 10.0, max_reps: int = 50) -> dict:
+    """The reference's FP32 oracle on the host cores, on a row sample of the
+    4096^3 workload, repeated for about `target_s` seconds."""
+    import torch
+
+    import oracle
+    from gb300_microbench_b200 import inputs
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    a, b = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM)
+    rows = 512
+    a_s = a[:rows]
+    oracle.gemm_reference_fp32(a_s, b)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.gemm_reference_fp32(a_s, b)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or reps >= max_reps:
+            break
+    flops = 2.0 * rows * N_DIM * K_DIM * reps
+    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x FP32 matmul of A rows [0,{rows}) (512x4096) by B^T (4096x4096) of the "
+                      f"4096^3 N(0,1) seed-0 workload, {el:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU path (FP32 matmul oracle)."""
+    if rank != 0:
+        return 0
+    import torch
+
+    import oracle
+    from gb300_microbench_b200 import inputs
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    a, b = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM)
+    # Size each step as a row sample of the 4096^3 workload so a step takes
+    # about a second on this host.
+    probe = a[:256]
+    t0 = time.perf_counter()
+    oracle.gemm_reference_fp32(probe, b)
+    t_probe = max(time.perf_counter() - t0, 1e-4)
+    rows = int(min(M_PER_RANK, max(256, 256 * (1.0 / t_probe))))
+    rows = max(256, rows // 256 * 256)
+    a_s = a[:rows]
+    for _ in range(args.warmup):
+        oracle.gemm_reference_fp32(a_s, b)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.gemm_reference_fp32(a_s, b)
+        times.append(time.perf_counter() - t0)
+    ms = 1000.0 * statistics.mean(times)
+    value = 2.0 * rows * N_DIM * K_DIM / (ms / 1000.0) / 1e12
+    sample = f"FP32 torch.matmul of A rows [0,{rows}) x B^T per step (4096x4096x4096 N(0,1) seed-0 workload)"
+    line = {
+        "metric": "bf16_gemm_tflops_per_gpu", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "gemm_bf16_config0_4096x4096x4096", "rows_per_step": rows,
+                   "path": "FP32 matmul oracle of gemm_comparison.py:2698-2715 on the host cores"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    from gb300_microbench_b200 import _native as nat
+    from gb300_microbench_b200 import inputs
+    from gb300_microbench_b200.gemm import CublasLtPlan, GemmPlan
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    # Rank r's shard of the global (4096 * world) x 4096 problem: the A row
+    # block is drawn with a per-rank seed, B is the same on every rank.
+    a_cpu, b_cpu = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM, seed=0)
+    if rank > 0:
+        g = torch.Generator().manual_seed(1000 + rank)
+        a_cpu = torch.randn(M_PER_RANK, K_DIM, generator=g).to(torch.bfloat16)
+    a = a_cpu.to(dev)
+    b = b_cpu.to(dev)
+    c = torch.empty(M_PER_RANK, N_DIM, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flops = 2.0 * M_PER_RANK * N_DIM * K_DIM
+
+    plan = GemmPlan(a, b, c, variant=args.variant, stream=stream)
+
+    def timed_steps(fn, steps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        stream.synchronize()
+        return [e0.elapsed_time(e1) for e0, e1 in evs]
+
+    # Correctness gate before timing: the oracle on a row block of C.
+    plan.run()
+    plan.synchronize()
+    import oracle
+
+    ref = oracle.gemm_reference_fp32(a_cpu[:256], b_cpu)
+    err = oracle.rel_frobenius(c[:256].float().cpu(), ref)
+    if err > 1e-2:
+        raise SystemExit(f"bench: GEMM result check failed (rel Frobenius {err:.3e} > 1e-2)")
+
+    for _ in range(args.warmup):
+        plan.run()
+    plan.synchronize()
+
+    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[0])
+                           if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local)
+    launches0 = nat.kernel_launches()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    step_ms = timed_steps(plan.run, args.steps)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    launches = nat.kernel_launches() - launches0
+    plan.synchronize()
+    ms_local = statistics.mean(step_ms)
+    ms = all_max(world, ms_local)
+    value = world * flops / (ms / 1000.0) / 1e12
+
+    # Hot-cache back-to-back figure (the reference's own timing method,
+    # gemm_comparison.py:3048-3067), reported beside the flushed one.
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    plan.run(args.steps)
+    e1.record(stream)
+    stream.synchronize()
+    hot_ms = all_max(world, e0.elapsed_time(e1) / args.steps)
+
+    # cuBLASLt on the same operands, same timing.
+    cublas = None
+    if not args.no_cublaslt:
+        c2 = torch.empty_like(c)
+        cmp = CublasLtPlan(a, b, c2, autotune=False, stream=stream)
+        cmp.run(args.warmup)
+        cl_ms = all_max(world, statistics.mean(timed_steps(cmp.run, args.steps)))
+        e0.record(stream)
+        cmp.run(args.steps)
+        e1.record(stream)
+        stream.synchronize()
+        cl_hot = all_max(world, e0.elapsed_time(e1) / args.steps)
+        cublas = {"tflops": world * flops / (cl_ms / 1000.0) / 1e12, "ms_per_step": cl_ms,
+                  "hot_tflops": world * flops / (cl_hot / 1000.0) / 1e12, "algo_index": cmp.algo_index,
+                  "ratio_ours_vs_cublaslt": cl_ms / ms, "ratio_hot": cl_hot / hot_ms}
+        cmp.close()
+        del c2
+
+    # End to end through the C ABI with host buffers.
+    a_h = a_cpu.pin_memory()
+    b_h = b_cpu.pin_memory()
+    c_h = torch.empty(M_PER_RANK, N_DIM, dtype=torch.bfloat16).pin_memory()
+    a_d = torch.empty_like(a)
+    b_d = torch.empty_like(b)
+    c_d = torch.empty_like(c)
+    eplan = GemmPlan(a_d, b_d, c_d, variant=args.variant, stream=stream)
+    for _ in range(2):
+        eplan.run_host(a_h, b_h, c_h)
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier(world)
+    t_e2e = []
+    for _ in range(e2e_steps):
+        t0 = time.perf_counter()
+        eplan.run_host(a_h, b_h, c_h)
+        t_e2e.append(time.perf_counter() - t0)
+    e2e_s = all_max(world, statistics.mean(t_e2e))
+    if not torch.equal(c_h[:256], c[:256].cpu()):
+        raise SystemExit("bench: end-to-end result differs from the device-path result")
+    h2d = a_h.numel() * 2 + b_h.numel() * 2
+    d2h = c_h.numel() * 2
+    eplan.close()
+
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    achieved = flops / (ms_local / 1000.0) / 1e12
+    traffic = committed_traffic()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_matmul_sample()
+
+    if rank == 0:
+        line = {
+            "metric": "bf16_gemm_tflops_per_gpu", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "gemm_bf16_config0_4096x4096x4096", "m_per_rank": M_PER_RANK, "n": N_DIM,
+                       "k": K_DIM, "global_m": M_PER_RANK * world, "variant": args.variant,
+                       "c_dtype": "bf16", "inputs": "N(0,1) BF16, torch.Generator seed 0 (rank>0: seed 1000+rank)",
+                       "l2": "flushed before every step (256 MiB write, outside the events)",
+                       "parallelism": f"rowshard{world}", "plan": plan.info},
+            "hot_cache_tflops": world * flops / (hot_ms / 1000.0) / 1e12,
+            "cublaslt": cublas,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{pk_kind} bf16_tflops (burst cuBLAS bf16 8192^3)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1000.0,
+                    "path": "bb_gemm_run_host (pinned host A, B -> device, GEMM, C -> pinned host)"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "check": {"rel_frobenius_rows_0_256": err},
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,241 @@
+// C ABI of the sm_100a GEMM: plan create / execute / run_host / destroy.
+// Mirrors the plan life cycle of the reference's cuBLASLt bridge
+// (gemm_comparison/cublaslt_bridge.cu:563-1016) for our own kernel.
+#include <atomic>
+#include <new>
+
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+
+namespace bb {
+std::atomic<int64_t> g_kernel_launches{0};
+}
+
+struct bb_gemm_plan {
+  bb::gemm::Plan p;
+  int* status_dev = nullptr;
+};
+
+namespace {
+
+int build_maps(bb::gemm::Plan& pl) {
+  using namespace bb;
+  const uint64_t M = pl.m, N = pl.n, K = pl.k, L = pl.l;
+  {
+    const uint64_t dims[3] = {K, M, L};
+    const uint64_t strides[2] = {K * 2, M * K * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    int rc = encode_tiled(&pl.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, pl.a, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    if (rc != BB_OK) return rc;
+  }
+  {
+    const uint64_t dims[3] = {K, N, L};
+    const uint64_t strides[2] = {K * 2, N * K * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(pl.b_rows), 1};
+    int rc = encode_tiled(&pl.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, pl.b, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    if (rc != BB_OK) return rc;
+  }
+  {
+    const bool f32 = pl.c_dtype == BB_DTYPE_F32;
+    const uint64_t es = f32 ? 4 : 2;
+    const uint64_t dims[3] = {N, M, L};
+    const uint64_t strides[2] = {N * es, M * N * es};
+    const uint32_t box[3] = {static_cast<uint32_t>(pl.epi_cols), 32, 1};
+    int rc = encode_tiled(&pl.tm_c, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          static_cast<int>(es), 3, pl.c, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    if (rc != BB_OK) return rc;
+  }
+  return BB_OK;
+}
+
+void fill_info(const bb::gemm::Plan& p, bb_gemm_info* info) {
+  if (!info) return;
+  info->mma_tiler_m = p.tile_m;
+  info->mma_tiler_n = p.tile_n;
+  info->cluster_m = p.cg;
+  info->cluster_n = 1;
+  info->use_2cta_instrs = p.cg == 2 ? 1 : 0;
+  info->max_active_clusters = p.max_active_clusters;
+  info->stages = p.stages;
+  info->grid_ctas = p.grid;
+  info->num_tiles = p.num_tiles;
+  info->smem_bytes = p.smem_bytes;
+  info->tmem_columns = p.tmem_cols;
+  info->threads_per_cta = 192;
+  info->persistent = p.persistent ? 1 : 0;
+  info->raster_group_m = p.group_m;
+  info->c_dtype = p.c_dtype;
+  info->variant = p.variant;
+}
+
+}  // namespace
+
+extern "C" {
+
+BB_API size_t bb_gemm_info_size(void) { return sizeof(bb_gemm_info); }
+
+BB_API int bb_gemm_plan_create(int64_t m, int64_t n, int64_t k, int64_t l, const void* a, const void* b, void* c,
+                               int a_dtype, int b_dtype, int c_dtype, int variant, void* stream,
+                               bb_gemm_plan** plan, bb_gemm_info* info) {
+  using namespace bb;
+  try {
+    clear_error();
+    if (!plan) {
+      set_error("bb_gemm_plan_create: plan out-pointer is null");
+      return BB_ERR_ARGUMENT;
+    }
+    *plan = nullptr;
+    if (m <= 0 || n <= 0 || k <= 0 || l <= 0) {
+      set_error("bb_gemm_plan_create: extents must be positive (m=%lld n=%lld k=%lld l=%lld)", (long long)m,
+                (long long)n, (long long)k, (long long)l);
+      return BB_ERR_ARGUMENT;
+    }
+    if (m * l > (int64_t(1) << 31) || n * l > (int64_t(1) << 31) || k > (int64_t(1) << 31)) {
+      set_error("bb_gemm_plan_create: extents exceed the 32-bit tile coordinate range");
+      return BB_ERR_ARGUMENT;
+    }
+    if (a_dtype != BB_DTYPE_BF16 || b_dtype != BB_DTYPE_BF16) {
+      set_error("bb_gemm_plan_create: A and B must be BF16");
+      return BB_ERR_UNSUPPORTED;
+    }
+    if (c_dtype != BB_DTYPE_BF16 && c_dtype != BB_DTYPE_F32) {
+      set_error("bb_gemm_plan_create: C must be BF16 or FP32");
+      return BB_ERR_UNSUPPORTED;
+    }
+    if (variant < BB_VARIANT_NONPERSISTENT_1CTA || variant > BB_VARIANT_TUNED) {
+      set_error("bb_gemm_plan_create: unknown variant %d", variant);
+      return BB_ERR_ARGUMENT;
+    }
+    if (k % 8 != 0) {
+      set_error("bb_gemm_plan_create: K=%lld must be a multiple of 8 (16-byte TMA row stride)", (long long)k);
+      return BB_ERR_ARGUMENT;
+    }
+    if ((c_dtype == BB_DTYPE_BF16 && n % 8 != 0) || (c_dtype == BB_DTYPE_F32 && n % 4 != 0)) {
+      set_error("bb_gemm_plan_create: N=%lld breaks the 16-byte row stride of C", (long long)n);
+      return BB_ERR_ARGUMENT;
+    }
+    DeviceInfo dev;
+    int rc = query_device(&dev);
+    if (rc != BB_OK) return rc;
+
+    auto* h = new (std::nothrow) bb_gemm_plan();
+    if (!h) {
+      set_error("bb_gemm_plan_create: out of host memory");
+      return BB_ERR_INTERNAL;
+    }
+    gemm::Plan& p = h->p;
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.l = l;
+    p.a = a;
+    p.b = b;
+    p.c = c;
+    p.c_dtype = c_dtype;
+    p.stream = static_cast<cudaStream_t>(stream);
+    rc = gemm::plan_init(p, variant, dev.sm_count);
+    if (rc == BB_OK) rc = build_maps(p);
+    if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
+    if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
+    if (rc != BB_OK) {
+      if (h->status_dev) cudaFree(h->status_dev);
+      delete h;
+      return rc;
+    }
+    p.status = h->status_dev;
+    fill_info(p, info);
+    *plan = h;
+    return BB_OK;
+  } catch (...) {
+    bb::set_error("bb_gemm_plan_create: unexpected C++ exception");
+    return BB_ERR_INTERNAL;
+  }
+}
+
+BB_API int bb_gemm_execute_n(bb_gemm_plan* plan, int iterations) {
+  using namespace bb;
+  try {
+    if (!plan || !plan->p.launch) {
+      set_error("bb_gemm_execute: null plan");
+      return BB_ERR_ARGUMENT;
+    }
+    for (int i = 0; i < iterations; ++i) {
+      int rc = plan->p.launch(plan->p);
+      if (rc != BB_OK) return rc;
+      ++plan->p.launches;
+      g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    return BB_OK;
+  } catch (...) {
+    bb::set_error("bb_gemm_execute: unexpected C++ exception");
+    return BB_ERR_INTERNAL;
+  }
+}
+
+BB_API int bb_gemm_execute(bb_gemm_plan* plan) { return bb_gemm_execute_n(plan, 1); }
+
+BB_API int bb_gemm_synchronize(bb_gemm_plan* plan) {
+  using namespace bb;
+  try {
+    if (!plan) {
+      set_error("bb_gemm_synchronize: null plan");
+      return BB_ERR_ARGUMENT;
+    }
+    BB_CUDA_TRY(cudaStreamSynchronize(plan->p.stream));
+    int st = 0;
+    BB_CUDA_TRY(cudaMemcpy(&st, plan->status_dev, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != 0) {
+      set_error("GEMM kernel reported device status 0x%x (%s)", st,
+                st == 0x200 ? "launch contract violated" : "a bounded wait timed out");
+      return st == 0x200 ? BB_ERR_INTERNAL : BB_ERR_TIMEOUT;
+    }
+    return BB_OK;
+  } catch (...) {
+    bb::set_error("bb_gemm_synchronize: unexpected C++ exception");
+    return BB_ERR_INTERNAL;
+  }
+}
+
+BB_API int bb_gemm_run_host(bb_gemm_plan* plan, const void* a_host, const void* b_host, void* c_host) {
+  using namespace bb;
+  try {
+    if (!plan || !a_host || !b_host || !c_host) {
+      set_error("bb_gemm_run_host: null argument");
+      return BB_ERR_ARGUMENT;
+    }
+    gemm::Plan& p = plan->p;
+    const size_t a_bytes = static_cast<size_t>(p.m) * p.k * p.l * 2;
+    const size_t b_bytes = static_cast<size_t>(p.n) * p.k * p.l * 2;
+    const size_t c_bytes = static_cast<size_t>(p.m) * p.n * p.l * (p.c_dtype == BB_DTYPE_F32 ? 4 : 2);
+    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.a), a_host, a_bytes, cudaMemcpyHostToDevice, p.stream));
+    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, p.stream));
+    int rc = bb_gemm_execute_n(plan, 1);
+    if (rc != BB_OK) return rc;
+    BB_CUDA_TRY(cudaMemcpyAsync(c_host, p.c, c_bytes, cudaMemcpyDeviceToHost, p.stream));
+    return bb_gemm_synchronize(plan);
+  } catch (...) {
+    bb::set_error("bb_gemm_run_host: unexpected C++ exception");
+    return BB_ERR_INTERNAL;
+  }
+}
+
+BB_API int64_t bb_gemm_launches(const bb_gemm_plan* plan) { return plan ? plan->p.launches : -1; }
+
+BB_API int bb_gemm_destroy(bb_gemm_plan* plan) {
+  using namespace bb;
+  if (!plan) return BB_OK;
+  int rc = BB_OK;
+  if (plan->status_dev) {
+    cudaError_t e = cudaFree(plan->status_dev);
+    if (e != cudaSuccess) rc = check_cuda(e, "cudaFree(status)");
+  }
+  delete plan;
+  return rc;
+}
+
+BB_API int64_t bb_kernel_launches(void) { return bb::g_kernel_launches.load(); }
+
+}  // extern "C"

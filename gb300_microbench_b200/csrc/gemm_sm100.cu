@@ -1,0 +1,447 @@
+// Persistent, warp-specialised dense GEMM for sm_100a:
+//   C[l] (M x N, BF16 or FP32) = A[l] (M x K, BF16, K-major) * B[l]^T (N x K, BF16, K-major)
+//
+// This is the kernel that takes the three CuTe DSL candidate slots of the
+// reference driver (gemm_comparison/gemm_comparison.py:209-260:
+// nonpersistent_1cta, persistent_1cta, persistent_2cta) plus a tuned slot.
+//
+// Roles inside one CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: one lane streams A/B k-blocks (64 BF16 wide,
+//               128-byte swizzle) into a STAGES-deep shared-memory ring.
+//   warp 1      TMEM allocator for the CTA, and (in the MMA CTA of the
+//               cluster) the single-thread tcgen05.mma issuer accumulating
+//               FP32 in a double-buffered TMEM accumulator.
+//   warps 2-5   epilogue warpgroup: tcgen05.ld of its 32 TMEM lanes,
+//               conversion to BF16 (or FP32 pass-through), 128-byte-swizzled
+//               staging in shared memory and a TMA store per 32x128-byte box.
+//
+// CTA-pair mode (kCG == 2): a cluster of two CTAs computes a 256 x BN tile
+// with tcgen05.mma.cta_group::2. Each CTA TMA-loads its own 128 rows of A
+// and its own BN/2 rows of B into its own shared memory; both loads
+// complete on the full barrier of CTA rank 0, whose single thread issues the
+// MMAs and signals both CTAs' barriers with one tcgen05.commit each. Every
+// TMA load fetches from global memory into its own CTA only.
+//
+// The tile scheduler is static and persistent: cluster c processes tiles
+// c, c + nclusters, ... in a grouped raster order (group_m tile-rows swept
+// across all tile-columns) so the A rows and B columns a wave touches stay
+// in L2.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+#include "ptx.cuh"
+
+namespace bb {
+namespace gemm {
+
+struct Params {
+  int32_t m, n, k, l;
+  int32_t tiles_m, tiles_n;
+  int32_t num_tiles;
+  int32_t k_blocks;
+  int32_t group_m;
+  int* status;
+};
+
+constexpr int kThreads = 192;
+constexpr int kBK = 64;  // K elements per stage: one 128-byte swizzle row of BF16
+
+template <int kCG, int kBN, bool kOutF32>
+struct Cfg {
+  static constexpr int BM = 128;              // accumulator rows held by one CTA
+  static constexpr int TILE_M = BM * kCG;     // rows of one cluster tile
+  static constexpr int B_ROWS = kBN / kCG;    // B rows staged by one CTA
+  static constexpr int A_BYTES = BM * kBK * 2;
+  static constexpr int B_BYTES = B_ROWS * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_COLS = kOutF32 ? 32 : 64;  // C columns per 128-byte store row
+  static constexpr int EPI_BOX_BYTES = 32 * 128;      // 32 rows x 128 bytes
+  static constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
+  static constexpr int TMEM_COLS = 2 * kBN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in maximum per block
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(STAGES >= 2, "ring too shallow");
+  static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation size");
+  static_assert(kBN % EPI_COLS == 0, "epilogue chunking");
+  static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+  // MMA shape legality for kind::f16: M=128 needs N%16==0, 16<=N<=256;
+  // M=256 (cta_group::2) the same.
+  static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "UMMA N");
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& l, int& m_blk, int& n_blk) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  l = t / per_batch;
+  const int r = t - l * per_batch;
+  const int group_size = p.group_m * p.tiles_n;
+  const int g = r / group_size;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first_m);
+  const int local = r - g * group_size;
+  m_blk = first_m + local % gm;
+  n_blk = local / gm;
+}
+
+template <int kCG, int kBN, bool kOutF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    bb_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const __grid_constant__ CUtensorMap tm_c, const Params p) {
+  using C = Cfg<kCG, kBN, kOutF32>;
+  constexpr int STAGES = C::STAGES;
+
+  // Launch contract, checked before any barrier, TMEM or cluster operation.
+  const uint32_t rank = (kCG == 2) ? cluster_ctarank() : 0u;
+  if (blockDim.x != kThreads || (kCG == 2 && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
+    if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kDevBadLaunch);
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * C::A_BYTES;
+  uint8_t* smem_epi = smem + STAGES * C::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + C::EPI_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tmem_full = bars + 2 * STAGES;
+  uint64_t* tmem_empty = bars + 2 * STAGES + 2;
+  uint64_t* mma_done = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const bool mma_cta = (kCG == 1) || (rank == 0);
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_c);
+  }
+  if (warp == 1 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tmem_full[a]), 1);
+      mbar_init(smem_u32(&tmem_empty[a]), 4 * kCG);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 1) {
+    tmem_alloc<kCG>(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish<kCG>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (kCG == 2) cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const int cluster_idx = blockIdx.x / kCG;
+  const int num_clusters = gridDim.x / kCG;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t full_target_rank = 0;
+      for (int t = cluster_idx; t < p.num_tiles && ok; t += num_clusters) {
+        int l, m_blk, n_blk;
+        tile_coords(p, t, l, m_blk, n_blk);
+        const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM;
+        const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_ROWS;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          if (mma_cta) mbar_arrive_expect_tx(fb, C::STAGE_BYTES * kCG);
+          const uint32_t da = smem_u32(smem_a + stage * C::A_BYTES);
+          const uint32_t db = smem_u32(smem_b + stage * C::B_BYTES);
+          if constexpr (kCG == 2) {
+            const uint32_t fbc = mapa_shared(fb, full_target_rank);
+            tma_load_3d_pair(da, &tm_a, fbc, kb * kBK, a_row, l);
+            tma_load_3d_pair(db, &tm_b, fbc, kb * kBK, b_row, l);
+          } else {
+            tma_load_3d(da, &tm_a, fb, kb * kBK, a_row, l);
+            tma_load_3d(db, &tm_b, fb, kb * kBK, b_row, l);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // Tail: wait until the MMA has released every stage, so no commit
+        // arrival can still be in flight towards this CTA when it exits.
+        for (int i = 0; i < STAGES; ++i) {
+          if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        // Aborted: let any TMA copy already issued land before teardown.
+        bounded_sleep_ns(2000000);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (mma_cta && lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(C::TILE_M, kBN);
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_iter = 0;
+      for (int t = cluster_idx; t < p.num_tiles && ok; t += num_clusters, ++acc_iter) {
+        const uint32_t acc = acc_iter & 1u;
+        const uint32_t acc_phase = (acc_iter >> 1) & 1u;
+        if (!bb_wait<kCG == 2>(smem_u32(&tmem_empty[acc]), acc_phase ^ 1u, p.status, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!bb_wait<kCG == 2>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_f16<kCG>(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32),
+                          idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty[stage]);
+          umma_commit<kCG>(eb);
+          if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(eb, 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&tmem_full[acc]);
+        umma_commit<kCG>(fb);
+        if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(fb, 1));
+      }
+      // Drain: every MMA issued so far must finish before TMEM is freed.
+      umma_commit<kCG>(smem_u32(mma_done));
+      bb_wait(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* ebuf = smem_epi + (warp - 2) * 2 * C::EPI_BOX_BYTES;
+    const uint32_t ebuf_u32 = smem_u32(ebuf);
+    uint32_t acc_iter = 0;
+    int chunk_seq = 0;
+    for (int t = cluster_idx; t < p.num_tiles; t += num_clusters, ++acc_iter) {
+      int l, m_blk, n_blk;
+      tile_coords(p, t, l, m_blk, n_blk);
+      const uint32_t acc = acc_iter & 1u;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1u;
+      if (!bb_wait<kCG == 2>(smem_u32(&tmem_full[acc]), acc_phase, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row0 = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
+      constexpr int kChunks = kBN / C::EPI_COLS;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c, ++chunk_seq) {
+        uint32_t packed[32];
+        if constexpr (kOutF32) {
+          tmem_ld_32x32b_x32(t_row + c * 32, packed);
+          tmem_ld_wait();
+        } else {
+          uint32_t lo[32], hi[32];
+          tmem_ld_32x32b_x32(t_row + c * 64, lo);
+          tmem_ld_32x32b_x32(t_row + c * 64 + 32, hi);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            packed[j] = pack_bf16x2(__uint_as_float(lo[2 * j]), __uint_as_float(lo[2 * j + 1]));
+            packed[16 + j] = pack_bf16x2(__uint_as_float(hi[2 * j]), __uint_as_float(hi[2 * j + 1]));
+          }
+        }
+        if (c == kChunks - 1) {
+          // Accumulator fully read into registers: hand it back to the MMA.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t eb = smem_u32(&tmem_empty[acc]);
+            if constexpr (kCG == 2) {
+              mbar_arrive_cluster(mapa_shared(eb, 0));
+            } else {
+              mbar_arrive(eb);
+            }
+          }
+        }
+        const uint32_t buf = ebuf_u32 + (chunk_seq & 1) * C::EPI_BOX_BYTES;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                       packed[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int col0 = n_blk * kBN + c * C::EPI_COLS;
+        if (lane == 0 && row0 < p.m && col0 < p.n) {
+          // Boxes that start inside C are clipped by TMA at the far edges;
+          // boxes wholly outside C (ragged last tile) are skipped.
+          tma_store_3d(&tm_c, buf, col0, row0, l);
+        }
+        if (lane == 0) bulk_commit_group();
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (kCG == 2) cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc<kCG>(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+struct KernelChoice {
+  int cg;
+  int bn;
+  bool persistent;
+  int group_m;
+};
+
+static KernelChoice choose(int variant, int64_t m, int64_t n, int64_t k, int sm_count) {
+  switch (variant) {
+    case BB_VARIANT_NONPERSISTENT_1CTA: return {1, 128, false, 8};
+    case BB_VARIANT_PERSISTENT_1CTA: return {1, 128, true, 8};
+    case BB_VARIANT_PERSISTENT_2CTA: return {2, 128, true, 8};
+    default: break;
+  }
+  (void)k;
+  (void)sm_count;
+  // Tuned: 256 x 256 pair tiles everywhere they fill the machine.
+  if (n >= 256 && m >= 256) return {2, 256, true, 8};
+  return {1, 128, true, 8};
+}
+
+template <int kCG, int kBN, bool kOutF32>
+static int launch(const Plan& pl) {
+  using C = Cfg<kCG, kBN, kOutF32>;
+  auto kern = bb_gemm_kernel<kCG, kBN, kOutF32>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = pl.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Params prm{};
+  prm.m = static_cast<int32_t>(pl.m);
+  prm.n = static_cast<int32_t>(pl.n);
+  prm.k = static_cast<int32_t>(pl.k);
+  prm.l = static_cast<int32_t>(pl.l);
+  prm.tiles_m = pl.tiles_m;
+  prm.tiles_n = pl.tiles_n;
+  prm.num_tiles = pl.num_tiles;
+  prm.k_blocks = pl.k_blocks;
+  prm.group_m = pl.group_m;
+  prm.status = pl.status;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, pl.tm_a, pl.tm_b, pl.tm_c, prm), "cudaLaunchKernelEx(gemm)");
+}
+
+template <int kCG, int kBN, bool kOutF32>
+static int prepare(Plan& pl, int sm_count) {
+  using C = Cfg<kCG, kBN, kOutF32>;
+  auto kern = bb_gemm_kernel<kCG, kBN, kOutF32>;
+  BB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+  if (kCG == 2) {
+    BB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+  }
+  pl.tile_m = C::TILE_M;
+  pl.tile_n = kBN;
+  pl.stages = C::STAGES;
+  pl.smem_bytes = C::SMEM_BYTES;
+  pl.tmem_cols = C::TMEM_COLS;
+  pl.b_rows = C::B_ROWS;
+  pl.epi_cols = C::EPI_COLS;
+  pl.tiles_m = static_cast<int>((pl.m + C::TILE_M - 1) / C::TILE_M);
+  pl.tiles_n = static_cast<int>((pl.n + kBN - 1) / kBN);
+  pl.num_tiles = pl.tiles_m * pl.tiles_n * static_cast<int>(pl.l);
+  pl.k_blocks = static_cast<int>((pl.k + kBK - 1) / kBK);
+  // Clusters that can be resident at once.
+  int max_clusters = sm_count / kCG;
+  {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(kCG * max_clusters), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n_clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&n_clusters, kern, &cfg) == cudaSuccess && n_clusters > 0) {
+      max_clusters = n_clusters;
+    } else {
+      cudaGetLastError();
+    }
+  }
+  pl.max_active_clusters = max_clusters;
+  const int clusters = pl.persistent ? (pl.num_tiles < max_clusters ? pl.num_tiles : max_clusters) : pl.num_tiles;
+  pl.grid = clusters * kCG;
+  pl.launch = &launch<kCG, kBN, kOutF32>;
+  return BB_OK;
+}
+
+int plan_init(Plan& pl, int variant, int sm_count) {
+  const KernelChoice ch = choose(variant, pl.m, pl.n, pl.k, sm_count);
+  pl.cg = ch.cg;
+  pl.persistent = ch.persistent;
+  pl.group_m = ch.group_m;
+  pl.variant = variant;
+  const bool f32 = pl.c_dtype == BB_DTYPE_F32;
+  int rc = BB_ERR_INTERNAL;
+  if (ch.cg == 1 && ch.bn == 128) rc = f32 ? prepare<1, 128, true>(pl, sm_count) : prepare<1, 128, false>(pl, sm_count);
+  else if (ch.cg == 1 && ch.bn == 256) rc = f32 ? prepare<1, 256, true>(pl, sm_count) : prepare<1, 256, false>(pl, sm_count);
+  else if (ch.cg == 2 && ch.bn == 128) rc = f32 ? prepare<2, 128, true>(pl, sm_count) : prepare<2, 128, false>(pl, sm_count);
+  else if (ch.cg == 2 && ch.bn == 256) rc = f32 ? prepare<2, 256, true>(pl, sm_count) : prepare<2, 256, false>(pl, sm_count);
+  if (rc == BB_ERR_INTERNAL) set_error("no kernel for cta_group=%d bn=%d", ch.cg, ch.bn);
+  return rc;
+}
+
+}  // namespace gemm
+}  // namespace bb

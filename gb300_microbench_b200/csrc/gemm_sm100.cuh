@@ -1,0 +1,35 @@
+// Internal plan of the sm_100a GEMM (see gemm_sm100.cu); the C ABI in
+// gemm_capi.cu wraps it as the opaque bb_gemm_plan.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace bb {
+namespace gemm {
+
+struct Plan {
+  int64_t m = 0, n = 0, k = 0, l = 0;
+  const void* a = nullptr;
+  const void* b = nullptr;
+  void* c = nullptr;
+  int c_dtype = 0;
+  int variant = 0;
+  cudaStream_t stream = nullptr;
+  CUtensorMap tm_a{}, tm_b{}, tm_c{};
+  int cg = 1, tile_m = 0, tile_n = 0, stages = 0, smem_bytes = 0, tmem_cols = 0, b_rows = 0, epi_cols = 0;
+  int tiles_m = 0, tiles_n = 0, num_tiles = 0, k_blocks = 0, group_m = 8, max_active_clusters = 0, grid = 0;
+  bool persistent = true;
+  int* status = nullptr;  // device word: 0, or the code of a timed-out wait
+  int64_t launches = 0;
+  int (*launch)(const Plan&) = nullptr;
+};
+
+// Picks the kernel for `variant` and fills the launch geometry (needs m, n,
+// k, l, c_dtype set). Returns a BB_* status.
+int plan_init(Plan& pl, int variant, int sm_count);
+
+}  // namespace gemm
+}  // namespace bb

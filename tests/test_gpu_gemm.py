@@ -1,0 +1,137 @@
+"""GEMM parity on the GPU through the C ABI, against the CPU oracle.
+
+Reference mode (integer operands, FP32 C) must be exact; the reference's
+elementwise check (|d| <= 0.1 + 1e-5 |ref|, gemm_comparison.py:2718-2755) is
+applied as well. BASELINE mode (N(0,1) operands, BF16 C) must be within a
+relative Frobenius error of 1e-2 of the FP32 oracle.
+"""
+import pytest
+import torch
+
+import oracle
+from gb300_microbench_b200 import inputs
+from gb300_microbench_b200.gemm import VARIANTS, CublasLtPlan, GemmPlan
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2  # relative Frobenius
+
+
+def _run(a, b, out_dtype, variant, dev):
+    l = a.shape[0] if a.dim() == 3 else None
+    ad, bd = a.to(dev).contiguous(), b.to(dev).contiguous()
+    shape = (*a.shape[:-1], b.shape[-2])
+    c = torch.full(shape, float("nan"), dtype=out_dtype, device=dev)
+    plan = GemmPlan(ad, bd, c, variant=variant)
+    plan.run()
+    plan.synchronize()
+    plan.close()
+    return c.cpu()
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("mnk", [(256, 256, 128), (512, 768, 320), (300, 264, 200), (128, 128, 64),
+                                 (1024, 512, 1024)])
+def test_reference_mode_exact(cuda_device, variant, mnk):
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0], b[0]
+    c = _run(a, b, torch.float32, variant, cuda_device)
+    ref = torch.from_numpy(oracle.gemm_ref_small(a.view(torch.int16).numpy().view("uint16"),
+                                                 b.view(torch.int16).numpy().view("uint16")))
+    assert torch.isfinite(c).all(), "unwritten (NaN) output elements"
+    assert torch.equal(c, ref)
+    bad, max_abs, _ = oracle.validate_elementwise(c.numpy(), ref.numpy())
+    assert bad == 0 and max_abs == 0.0
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("mnk", [(256, 256, 256), (384, 640, 448), (1000, 1000, 1000)])
+def test_baseline_mode_bf16(cuda_device, variant, mnk):
+    m, n, k = mnk
+    a, b = inputs.baseline_mode_operands(m, n, k)
+    c = _run(a, b, torch.bfloat16, variant, cuda_device)
+    ref = oracle.gemm_reference_fp32(a, b)
+    assert torch.isfinite(c.float()).all()
+    err = oracle.rel_frobenius(c.float(), ref)
+    assert err <= BF16_TOL, err
+    # BF16 rounding of the output alone gives ~2e-3; a layout bug gives ~1.
+    assert err < 5e-3
+
+
+@pytest.mark.parametrize("variant", ["persistent_2cta", "tuned", "persistent_1cta"])
+def test_batched_l2(cuda_device, variant):
+    a, b = inputs.reference_mode_operands(384, 512, 256, l=2)
+    c = _run(a, b, torch.float32, variant, cuda_device)
+    for i in range(2):
+        ref = oracle.gemm_reference_fp32(a[i], b[i])
+        assert torch.equal(c[i], ref)
+
+
+@pytest.mark.parametrize("variant", ["tuned", "persistent_2cta"])
+def test_full_size_4096_baseline(cuda_device, variant):
+    """Config 0 at full size: 4096^3, N(0,1) seed 0, BF16 C."""
+    a, b = inputs.baseline_mode_operands(4096, 4096, 4096)
+    c = _run(a, b, torch.bfloat16, variant, cuda_device)
+    ref = oracle.gemm_reference_fp32(a, b)
+    err = oracle.rel_frobenius(c.float(), ref)
+    assert err <= BF16_TOL, err
+
+
+def test_repeat_launches_idempotent(cuda_device):
+    """Back-to-back launches of one plan rewrite the same C (persistent
+    scheduler, TMEM double buffer and ring phases all restart per launch)."""
+    a, b = inputs.baseline_mode_operands(2048, 1536, 1024)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    c = torch.empty(2048, 1536, dtype=torch.bfloat16, device=cuda_device)
+    plan = GemmPlan(ad, bd, c, variant="tuned")
+    plan.run()
+    plan.synchronize()
+    first = c.clone()
+    plan.run(5)
+    plan.synchronize()
+    assert torch.equal(first, c)
+    assert plan.launches == 6
+
+
+def test_skinny_shapes_reference_mode(cuda_device):
+    """The three skinny shapes of the sweep, scaled down in K (exact check)."""
+    for m, n, k in [(16384, 512, 256), (512, 16384, 256), (4096, 512, 512)]:
+        a, b = inputs.reference_mode_operands(m, n, k)
+        c = _run(a[0], b[0], torch.float32, "tuned", cuda_device)
+        ref = oracle.gemm_reference_fp32(a[0], b[0])
+        assert torch.equal(c, ref), (m, n, k)
+
+
+def test_run_host_matches_device_path(cuda_device):
+    a, b = inputs.baseline_mode_operands(512, 512, 512)
+    ad = torch.empty_like(a, device=cuda_device)
+    bd = torch.empty_like(b, device=cuda_device)
+    c = torch.empty(512, 512, dtype=torch.bfloat16, device=cuda_device)
+    plan = GemmPlan(ad, bd, c)
+    c_host = torch.empty(512, 512, dtype=torch.bfloat16).pin_memory()
+    plan.run_host(a.pin_memory(), b.pin_memory(), c_host)
+    ref = _run(a, b, torch.bfloat16, "tuned", cuda_device)
+    assert torch.equal(c_host, ref)
+
+
+def test_cublaslt_comparator_agrees(cuda_device):
+    a, b = inputs.baseline_mode_operands(1024, 1024, 1024)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    c = torch.empty(1024, 1024, dtype=torch.float32, device=cuda_device)
+    cmp = CublasLtPlan(ad, bd, c)
+    cmp.run()
+    torch.cuda.synchronize()
+    ref = oracle.gemm_reference_fp32(a, b)
+    assert oracle.rel_frobenius(c.cpu(), ref) < 1e-5
+
+
+def test_bad_arguments_rejected(cuda_device):
+    from gb300_microbench_b200 import _native as nat
+
+    a = torch.zeros(128, 100, dtype=torch.bfloat16, device=cuda_device)  # K not a multiple of 8
+    b = torch.zeros(128, 100, dtype=torch.bfloat16, device=cuda_device)
+    c = torch.zeros(128, 128, dtype=torch.bfloat16, device=cuda_device)
+    with pytest.raises(nat.NativeCallError) as ei:
+        GemmPlan(a, b, c)
+    assert ei.value.status == nat.BB_ERR_ARGUMENT
