@@ -47,7 +47,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on BASELINE config 0 (4096^3 per GPU)")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--variant", default="tuned")
@@ -83,59 +83,68 @@ def committed_traffic():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while running."""
+    """Samples the SM clock and the throttle reasons through NVML every
+    ~2 ms on a background thread while the timed region runs."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
+    }
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.device_index = device_index
+        self.period_s = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
         self._t = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # NVML missing: report it, do not fail the bench
+            self.error = f"nvml unavailable: {exc}"
             return
-        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((sm, rs))
+            except Exception as exc:
+                self.error = str(exc)
+                return
+            time.sleep(self.period_s)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
         if self._t:
             self._t.join(timeout=2)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": self.error or "no samples"}
+        reasons = sorted({name for _, rs in self.samples for name, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "NVML, 2 ms period"}
+
+
+def gpu_index_for(local: int) -> int:
+    """NVML index of this process's CUDA device (CUDA_VISIBLE_DEVICES aware)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [p.strip() for p in vis.split(",") if p.strip()]
+    if parts and all(p.isdigit() for p in parts) and local < len(parts):
+        return int(parts[local])
+    return local
 
 
 def dist_setup(args):
@@ -171,7 +180,7 @@ def all_max(world, value: float) -> float:
     return float(t.item())
 
 
-def cpu_matmul_sample(target_s: float = 10.0, max_reps: int = 50) -> dict:
+def cpu_matmul_sample(target_s: float = 10.0, max_reps: int = 5000) -> dict:
     """The reference's FP32 oracle on the host cores, on a row sample of the
     4096^3 workload, repeated for about `target_s` seconds."""
     import torch
@@ -293,8 +302,7 @@ def run_ours(args, world, rank, local):
         plan.run()
     plan.synchronize()
 
-    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[0])
-                           if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local)
+    sampler = ClockSampler(gpu_index_for(local if world > 1 else 0))
     launches0 = nat.kernel_launches()
     barrier(world)
     torch.cuda.synchronize()

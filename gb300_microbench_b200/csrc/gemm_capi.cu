@@ -140,8 +140,18 @@ BB_API int bb_gemm_plan_create(int64_t m, int64_t n, int64_t k, int64_t l, const
     if (rc == BB_OK) rc = build_maps(p);
     if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
     if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
+    if (rc == BB_OK && p.sk_parts > 0) {
+      // Stream-K workspace, owned by the plan (as the reference bridge owns
+      // its cuBLASLt workspace). Counters start at zero and are reset by the
+      // kernel after each use.
+      rc = check_cuda(cudaMalloc(&p.partials, p.partial_floats * sizeof(float)), "cudaMalloc(split-tail partials)");
+      if (rc == BB_OK) rc = check_cuda(cudaMalloc(&p.counters, p.counter_ints * sizeof(int)), "cudaMalloc(counters)");
+      if (rc == BB_OK) rc = check_cuda(cudaMemset(p.counters, 0, p.counter_ints * sizeof(int)), "cudaMemset(counters)");
+    }
     if (rc != BB_OK) {
       if (h->status_dev) cudaFree(h->status_dev);
+      if (p.partials) cudaFree(p.partials);
+      if (p.counters) cudaFree(p.counters);
       delete h;
       return rc;
     }
@@ -228,9 +238,11 @@ BB_API int bb_gemm_destroy(bb_gemm_plan* plan) {
   using namespace bb;
   if (!plan) return BB_OK;
   int rc = BB_OK;
-  if (plan->status_dev) {
-    cudaError_t e = cudaFree(plan->status_dev);
-    if (e != cudaSuccess) rc = check_cuda(e, "cudaFree(status)");
+  for (void* ptr : {static_cast<void*>(plan->status_dev), static_cast<void*>(plan->p.partials),
+                    static_cast<void*>(plan->p.counters)}) {
+    if (!ptr) continue;
+    cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess && rc == BB_OK) rc = check_cuda(e, "cudaFree(plan buffer)");
   }
   delete plan;
   return rc;

@@ -28,6 +28,9 @@
 // in L2.
 #include <cuda.h>
 
+#include <cmath>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "ptx.cuh"
@@ -41,8 +44,71 @@ struct Params {
   int32_t num_tiles;
   int32_t k_blocks;
   int32_t group_m;
+  int32_t num_clusters;
+  // Data-parallel tiles [0, dp_tiles) go to cluster t % num_clusters with
+  // the full K range. Each tile of the tail [dp_tiles, num_tiles) is split
+  // into sk_parts equal k-block ranges, all in one round: part j of tail
+  // tile t is the work of cluster t * sk_parts + j, after its data-parallel
+  // tiles (the host guarantees tail_tiles * sk_parts <= num_clusters).
+  int32_t dp_tiles;
+  int32_t sk_parts;  // 0: no split tail
+  float* partials;   // split-tail FP32 partial slices: (parts - 1) tile-sized areas per tail tile and CTA rank
+  int* counters;     // two counters (arrived, done) per tail tile and CTA rank
   int* status;
 };
+
+struct WorkItem {
+  int tile;
+  int kb0, kb1;  // k-block range [kb0, kb1)
+  int part;      // -1 for a whole tile, else the part index within the tile
+};
+
+// Work item `idx` of cluster c: its data-parallel tiles first, then its
+// parts of split tail tiles.
+__device__ __forceinline__ bool next_item(const Params& p, int c, int idx, WorkItem& it) {
+  const int n_dp = c < p.dp_tiles ? (p.dp_tiles - 1 - c) / p.num_clusters + 1 : 0;
+  if (idx < n_dp) {
+    it.tile = c + idx * p.num_clusters;
+    it.kb0 = 0;
+    it.kb1 = p.k_blocks;
+    it.part = -1;
+    return true;
+  }
+  if (p.sk_parts == 0 || idx != n_dp) return false;
+  const int n_parts = (p.num_tiles - p.dp_tiles) * p.sk_parts;
+  if (c >= n_parts) return false;
+  const int t_local = c / p.sk_parts;
+  const int j = c - t_local * p.sk_parts;
+  it.tile = p.dp_tiles + t_local;
+  it.kb0 = (j * p.k_blocks) / p.sk_parts;
+  it.kb1 = ((j + 1) * p.k_blocks) / p.sk_parts;
+  it.part = j;
+  return true;
+}
+
+// Bounded spin until *ctr >= target (acquire). Returns false on timeout or
+// when another role recorded an error.
+__device__ __forceinline__ bool spin_until_at_least(const int* ctr, int target, int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if ((++spins & 15u) == 0) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicCAS(status, 0, code);
+        return false;
+      }
+      if (*reinterpret_cast<volatile int*>(status) != 0) return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 constexpr int kThreads = 192;
 constexpr int kBK = 64;  // K elements per stage: one 128-byte swizzle row of BF16
@@ -113,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_empty = bars + 2 * STAGES + 2;
   uint64_t* mma_done = bars + 2 * STAGES + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* epi_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 6);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -145,8 +212,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
+  // Programmatic dependent launch: the set-up above (barrier init, TMEM
+  // allocation) overlaps the previous kernel in the stream; no global memory
+  // is touched before that kernel has completed. Dependents may launch now;
+  // their CTAs only become resident as this kernel's CTAs exit.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   const int cluster_idx = blockIdx.x / kCG;
-  const int num_clusters = gridDim.x / kCG;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -155,12 +228,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       const uint32_t full_target_rank = 0;
-      for (int t = cluster_idx; t < p.num_tiles && ok; t += num_clusters) {
+      WorkItem it;
+      for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx) {
         int l, m_blk, n_blk;
-        tile_coords(p, t, l, m_blk, n_blk);
+        tile_coords(p, it.tile, l, m_blk, n_blk);
         const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM;
         const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_ROWS;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
@@ -206,7 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_iter = 0;
-      for (int t = cluster_idx; t < p.num_tiles && ok; t += num_clusters, ++acc_iter) {
+      WorkItem it;
+      for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx, ++acc_iter) {
         const uint32_t acc = acc_iter & 1u;
         const uint32_t acc_phase = (acc_iter >> 1) & 1u;
         if (!bb_wait<kCG == 2>(smem_u32(&tmem_empty[acc]), acc_phase ^ 1u, p.status, kDevTimeoutMma)) {
@@ -215,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!bb_wait<kCG == 2>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
@@ -226,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             umma_f16<kCG>(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32),
-                          idesc, (kb | kk) != 0 ? 1u : 0u);
+                          idesc, (kb != it.kb0 || kk != 0) ? 1u : 0u);
           }
           const uint32_t eb = smem_u32(&empty[stage]);
           umma_commit<kCG>(eb);
@@ -248,68 +323,193 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ep_tid = threadIdx.x - 64;  // 0..127 within the epilogue warpgroup
     uint8_t* ebuf = smem_epi + (warp - 2) * 2 * C::EPI_BOX_BYTES;
     const uint32_t ebuf_u32 = smem_u32(ebuf);
     uint32_t acc_iter = 0;
     int chunk_seq = 0;
-    for (int t = cluster_idx; t < p.num_tiles; t += num_clusters, ++acc_iter) {
+    constexpr int kChunks = kBN / C::EPI_COLS;
+
+    // Stages one 32-row x 128-byte chunk in swizzled shared memory and
+    // stores it to C with TMA.
+    auto store_chunk = [&](const uint32_t (&packed)[32], int row0, int col0, int l) {
+      const uint32_t buf = ebuf_u32 + (chunk_seq & 1) * C::EPI_BOX_BYTES;
+      ++chunk_seq;
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                     packed[4 * j + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < p.m && col0 < p.n) {
+        // Boxes that start inside C are clipped by TMA at the far edges;
+        // boxes wholly outside C (ragged last tile) are skipped.
+        tma_store_3d(&tm_c, buf, col0, row0, l);
+      }
+      if (lane == 0) bulk_commit_group();
+    };
+    auto pack_chunk = [&](const float* v, uint32_t (&packed)[32]) {
+      if constexpr (kOutF32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) packed[j] = __float_as_uint(v[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+      }
+    };
+    auto release_acc = [&](uint32_t acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t eb = smem_u32(&tmem_empty[acc]);
+        if constexpr (kCG == 2) {
+          mbar_arrive_cluster(mapa_shared(eb, 0));
+        } else {
+          mbar_arrive(eb);
+        }
+      }
+    };
+
+    WorkItem it;
+    for (int idx = 0; next_item(p, cluster_idx, idx, it); ++idx, ++acc_iter) {
       int l, m_blk, n_blk;
-      tile_coords(p, t, l, m_blk, n_blk);
+      tile_coords(p, it.tile, l, m_blk, n_blk);
       const uint32_t acc = acc_iter & 1u;
       const uint32_t acc_phase = (acc_iter >> 1) & 1u;
       if (!bb_wait<kCG == 2>(smem_u32(&tmem_full[acc]), acc_phase, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const int row0 = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
-      constexpr int kChunks = kBN / C::EPI_COLS;
+      constexpr int ncols = kOutF32 ? 32 : 64;  // accumulator columns behind one 128-byte store row
+
+      if (it.part < 0) {
+        // ---- whole tile: TMEM -> registers -> C
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c, ++chunk_seq) {
-        uint32_t packed[32];
-        if constexpr (kOutF32) {
-          tmem_ld_32x32b_x32(t_row + c * 32, packed);
-          tmem_ld_wait();
-        } else {
-          uint32_t lo[32], hi[32];
-          tmem_ld_32x32b_x32(t_row + c * 64, lo);
-          tmem_ld_32x32b_x32(t_row + c * 64 + 32, hi);
+        for (int c = 0; c < kChunks; ++c) {
+          float v[64];
+          uint32_t r0[32];
+          tmem_ld_32x32b_x32(t_row + c * ncols, r0);
+          if constexpr (!kOutF32) {
+            uint32_t r1[32];
+            tmem_ld_32x32b_x32(t_row + c * ncols + 32, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(r1[j]);
+          } else {
+            tmem_ld_wait();
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+          if (c == kChunks - 1) release_acc(acc);  // accumulator now lives in registers
+          uint32_t packed[32];
+          pack_chunk(v, packed);
+          store_chunk(packed, row0, n_blk * kBN + c * C::EPI_COLS, l);
+        }
+      } else {
+        // ---- part j of a tile split in s along K. Columns are cut into s
+        // slices; part j writes its FP32 values of every slice but its own to
+        // the workspace, waits until all s parts have written, then sums
+        // slice j over the parts in part order (the same fixed order for
+        // every slice, so the result does not depend on timing) and stores
+        // it. Each block is laid out [col / 4][row][4] floats, so one warp
+        // access of a column quad covers 512 contiguous bytes.
+        const int t_local = it.tile - p.dp_tiles;
+        const int parts = p.sk_parts;
+        const int j = it.part;
+        const int row = q * 32 + lane;
+        const int slice = kBN / parts;  // multiple of 64: parts in {2, 4}, kBN 128 or 256
+        // Block (i, w): part w's values of column slice i (w != i), BM rows x
+        // slice columns; the tile's (parts - 1) * parts blocks are packed.
+        const int64_t tile_base = (static_cast<int64_t>(t_local) * kCG + rank) * (parts - 1) * (C::BM * kBN);
+        auto block_ptr = [&](int i, int w) {
+          const int idx = i * (parts - 1) + (w < i ? w : w - 1);
+          return reinterpret_cast<float4*>(p.partials + tile_base + static_cast<int64_t>(idx) * C::BM * slice) + row;
+        };
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          const int i = (c * 32) / slice;
+          if (i == j) continue;  // own slice stays in TMEM
+          float4* dst = block_ptr(i, j) + ((c * 32 - i * slice) / 4) * C::BM;
+          uint32_t r0[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r0);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            packed[j] = pack_bf16x2(__uint_as_float(lo[2 * j]), __uint_as_float(lo[2 * j + 1]));
-            packed[16 + j] = pack_bf16x2(__uint_as_float(hi[2 * j]), __uint_as_float(hi[2 * j + 1]));
+          for (int jj = 0; jj < 8; ++jj) {
+            __stcg(dst + jj * C::BM,
+                   make_float4(__uint_as_float(r0[4 * jj]), __uint_as_float(r0[4 * jj + 1]),
+                               __uint_as_float(r0[4 * jj + 2]), __uint_as_float(r0[4 * jj + 3])));
           }
         }
-        if (c == kChunks - 1) {
-          // Accumulator fully read into registers: hand it back to the MMA.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            const uint32_t eb = smem_u32(&tmem_empty[acc]);
-            if constexpr (kCG == 2) {
-              mbar_arrive_cluster(mapa_shared(eb, 0));
-            } else {
-              mbar_arrive(eb);
+        __threadfence();
+        named_bar_sync(1, 128);
+        int* arrived = p.counters + 2 * (t_local * kCG + static_cast<int>(rank));
+        int* done = arrived + 1;
+        if (ep_tid == 0) {
+          atomicAdd(arrived, 1);
+          epi_flag[0] = spin_until_at_least(arrived, parts, p.status, kDevTimeoutEpilogue) ? 1 : 0;
+          __threadfence();
+        }
+        named_bar_sync(1, 128);
+        const bool peers_ok = epi_flag[0] != 0;
+        if (peers_ok) {
+#pragma unroll 1
+          for (int c = j * slice / ncols; c < (j + 1) * slice / ncols; ++c) {
+            float own[64];
+            {
+              uint32_t r0[32];
+              tmem_ld_32x32b_x32(t_row + c * ncols, r0);
+              if constexpr (!kOutF32) {
+                uint32_t r1[32];
+                tmem_ld_32x32b_x32(t_row + c * ncols + 32, r1);
+                tmem_ld_wait();
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) own[32 + jj] = __uint_as_float(r1[jj]);
+              } else {
+                tmem_ld_wait();
+              }
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) own[jj] = __uint_as_float(r0[jj]);
             }
+            float v[64];
+#pragma unroll
+            for (int jj = 0; jj < ncols; ++jj) v[jj] = 0.0f;
+            for (int part = 0; part < parts; ++part) {
+              if (part == j) {
+#pragma unroll
+                for (int jj = 0; jj < ncols; ++jj) v[jj] += own[jj];
+                continue;
+              }
+              const float4* src = block_ptr(j, part) + ((c * ncols - j * slice) / 4) * C::BM;
+              float4 x[ncols / 4];
+#pragma unroll
+              for (int jj = 0; jj < ncols / 4; ++jj) x[jj] = __ldcg(src + jj * C::BM);
+#pragma unroll
+              for (int jj = 0; jj < ncols / 4; ++jj) {
+                v[4 * jj] += x[jj].x;
+                v[4 * jj + 1] += x[jj].y;
+                v[4 * jj + 2] += x[jj].z;
+                v[4 * jj + 3] += x[jj].w;
+              }
+            }
+            uint32_t packed[32];
+            pack_chunk(v, packed);
+            store_chunk(packed, row0, n_blk * kBN + c * C::EPI_COLS, l);
           }
         }
-        const uint32_t buf = ebuf_u32 + (chunk_seq & 1) * C::EPI_BOX_BYTES;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t row_addr = buf + lane * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                       packed[4 * j + 3]);
+        release_acc(acc);
+        named_bar_sync(1, 128);
+        if (ep_tid == 0 && peers_ok) {
+          // Every part has passed its wait: the last one resets both
+          // counters for the next launch.
+          if (atomicAdd(done, 1) == parts - 1) {
+            atomicExch(arrived, 0);
+            atomicExch(done, 0);
+          }
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        const int col0 = n_blk * kBN + c * C::EPI_COLS;
-        if (lane == 0 && row0 < p.m && col0 < p.n) {
-          // Boxes that start inside C are clipped by TMA at the far edges;
-          // boxes wholly outside C (ragged last tile) are skipped.
-          tma_store_3d(&tm_c, buf, col0, row0, l);
-        }
-        if (lane == 0) bulk_commit_group();
       }
     }
     if (lane == 0) bulk_wait_group<0>();
@@ -334,20 +534,21 @@ struct KernelChoice {
   int bn;
   bool persistent;
   int group_m;
+  bool stream_k;
 };
 
 static KernelChoice choose(int variant, int64_t m, int64_t n, int64_t k, int sm_count) {
   switch (variant) {
-    case BB_VARIANT_NONPERSISTENT_1CTA: return {1, 128, false, 8};
-    case BB_VARIANT_PERSISTENT_1CTA: return {1, 128, true, 8};
-    case BB_VARIANT_PERSISTENT_2CTA: return {2, 128, true, 8};
+    case BB_VARIANT_NONPERSISTENT_1CTA: return {1, 128, false, 8, false};
+    case BB_VARIANT_PERSISTENT_1CTA: return {1, 128, true, 8, false};
+    case BB_VARIANT_PERSISTENT_2CTA: return {2, 128, true, 8, false};
     default: break;
   }
   (void)k;
   (void)sm_count;
   // Tuned: 256 x 256 pair tiles everywhere they fill the machine.
-  if (n >= 256 && m >= 256) return {2, 256, true, 8};
-  return {1, 128, true, 8};
+  if (n >= 256 && m >= 256) return {2, 256, true, 8, true};
+  return {1, 128, true, 8, true};
 }
 
 template <int kCG, int kBN, bool kOutF32>
@@ -359,13 +560,15 @@ static int launch(const Plan& pl) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = pl.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kCG;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pl.pdl ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   Params prm{};
   prm.m = static_cast<int32_t>(pl.m);
   prm.n = static_cast<int32_t>(pl.n);
@@ -376,6 +579,11 @@ static int launch(const Plan& pl) {
   prm.num_tiles = pl.num_tiles;
   prm.k_blocks = pl.k_blocks;
   prm.group_m = pl.group_m;
+  prm.num_clusters = pl.grid / kCG;
+  prm.dp_tiles = pl.dp_tiles;
+  prm.sk_parts = pl.sk_parts;
+  prm.partials = pl.partials;
+  prm.counters = pl.counters;
   prm.status = pl.status;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, pl.tm_a, pl.tm_b, pl.tm_c, prm), "cudaLaunchKernelEx(gemm)");
 }
@@ -421,7 +629,40 @@ static int prepare(Plan& pl, int sm_count) {
     }
   }
   pl.max_active_clusters = max_clusters;
-  const int clusters = pl.persistent ? (pl.num_tiles < max_clusters ? pl.num_tiles : max_clusters) : pl.num_tiles;
+  int clusters = pl.persistent ? (pl.num_tiles < max_clusters ? pl.num_tiles : max_clusters) : pl.num_tiles;
+  pl.dp_tiles = pl.num_tiles;
+  pl.sk_parts = 0;
+  // BB_GEMM_STREAM_K=0 disables the split tail, =1 uses it whenever the
+  // last wave is partial (tuning override; unset: efficiency threshold and
+  // at least 48 k-blocks, below which the partial exchange costs more than
+  // the idle half tile it saves).
+  const char* sk_env = std::getenv("BB_GEMM_STREAM_K");
+  const int sk_mode = sk_env ? std::atoi(sk_env) : -1;
+  if (pl.stream_k && pl.persistent && (pl.k_blocks >= 48 || sk_mode == 1) && sk_mode != 0) {
+    // Split tail: when the last wave of whole tiles would leave clusters
+    // idle, each of the rem tail tiles is cut into s equal K parts, s = 4 or
+    // 2, the largest with rem * s <= P, so the tail takes about 1/s of a
+    // tile time plus the exchange of partial slices.
+    const int P = max_clusters;
+    const int full = pl.num_tiles / P;
+    const int rem = pl.num_tiles % P;
+    const double waves = static_cast<double>(full + (rem ? 1 : 0));
+    const double eff = static_cast<double>(pl.num_tiles) / (waves * P);
+    if (rem != 0 && (eff < 0.95 || sk_mode == 1)) {
+      // One round of parts only (every part of a tile runs at the same
+      // time, so the wait for peer parts is short and cannot form chains).
+      int sp = P / rem;
+      if (sp > 4) sp = 4;
+      if (sp == 3) sp = 2;  // slices must stay multiples of 64 columns
+      if (sp >= 2 && kBN / sp >= 64) {
+        clusters = P;
+        pl.dp_tiles = full * P;
+        pl.sk_parts = sp;
+        pl.partial_floats = static_cast<int64_t>(rem) * (sp - 1) * kCG * C::BM * kBN;
+        pl.counter_ints = static_cast<int64_t>(rem) * kCG * 2;
+      }
+    }
+  }
   pl.grid = clusters * kCG;
   pl.launch = &launch<kCG, kBN, kOutF32>;
   return BB_OK;
@@ -431,6 +672,10 @@ int plan_init(Plan& pl, int variant, int sm_count) {
   const KernelChoice ch = choose(variant, pl.m, pl.n, pl.k, sm_count);
   pl.cg = ch.cg;
   pl.persistent = ch.persistent;
+  // BB_GEMM_PDL=0 turns programmatic dependent launch off.
+  const char* pdl_env = std::getenv("BB_GEMM_PDL");
+  pl.pdl = !(pdl_env && std::atoi(pdl_env) == 0);
+  pl.stream_k = ch.stream_k;
   pl.group_m = ch.group_m;
   pl.variant = variant;
   const bool f32 = pl.c_dtype == BB_DTYPE_F32;

@@ -22,6 +22,14 @@ struct Plan {
   int cg = 1, tile_m = 0, tile_n = 0, stages = 0, smem_bytes = 0, tmem_cols = 0, b_rows = 0, epi_cols = 0;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, k_blocks = 0, group_m = 8, max_active_clusters = 0, grid = 0;
   bool persistent = true;
+  bool stream_k = false;
+  bool pdl = true;           // launch with programmatic stream serialisation
+  int dp_tiles = 0;          // tiles computed whole (data-parallel)
+  int sk_parts = 0;          // K parts per split tail tile (0: no split tail)
+  int64_t partial_floats = 0;  // workspace the split-tail tail needs
+  int64_t counter_ints = 0;
+  float* partials = nullptr;
+  int* counters = nullptr;
   int* status = nullptr;  // device word: 0, or the code of a timed-out wait
   int64_t launches = 0;
   int (*launch)(const Plan&) = nullptr;

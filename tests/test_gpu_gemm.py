@@ -135,3 +135,35 @@ def test_bad_arguments_rejected(cuda_device):
     with pytest.raises(nat.NativeCallError) as ei:
         GemmPlan(a, b, c)
     assert ei.value.status == nat.BB_ERR_ARGUMENT
+
+
+@pytest.mark.parametrize("mnk", [(4096, 4096, 1024), (16384, 512, 1024), (512, 16384, 1024), (2304, 2048, 4096),
+                                 (640, 768, 2048), (32768, 512, 4096), (256, 2560, 3072)])
+def test_split_tail_exact(cuda_device, mnk, monkeypatch):
+    """Shapes whose last wave is partial run a split tail (tail tiles cut in
+    2 or 4 along K) in the tuned variant; BB_GEMM_STREAM_K=1 forces it even
+    for short K. Integer operands make every split of K exact."""
+    monkeypatch.setenv("BB_GEMM_STREAM_K", "1")
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    c = _run(a[0], b[0], torch.float32, "tuned", cuda_device)
+    ref = oracle.gemm_reference_fp32(a[0], b[0])
+    assert torch.equal(c, ref)
+
+
+def test_split_tail_deterministic_bf16(cuda_device):
+    """The fix-up sums partials in a fixed order: repeated launches are
+    bit-identical even though arrival order varies."""
+    a, b = inputs.baseline_mode_operands(4096, 4096, 2048)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    c = torch.empty(4096, 4096, dtype=torch.bfloat16, device=cuda_device)
+    plan = GemmPlan(ad, bd, c, variant="tuned")
+    plan.run()
+    plan.synchronize()
+    first = c.clone()
+    for _ in range(3):
+        plan.run(3)
+        plan.synchronize()
+        assert torch.equal(first, c)
+    ref = oracle.gemm_reference_fp32(a, b)
+    assert oracle.rel_frobenius(c.cpu().float(), ref) <= BF16_TOL
