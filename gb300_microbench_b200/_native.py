@@ -103,6 +103,8 @@ BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_gemm_synchronize": (c_int, [c_void_p]),
     "bb_gemm_launches": (c_int64, [c_void_p]),
     "bb_gemm_destroy": (c_int, [c_void_p]),
+    "bb_gemm_run_noalloc": (c_int, [c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                                    c_void_p, c_int]),
     "bb_copy_info_size": (c_size_t, []),
     "bb_copy_plan": (c_int, [c_int, c_int, c_int, c_int, c_int64, c_int, POINTER(CopyInfo)]),
     "bb_copy_run": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,

@@ -16,9 +16,10 @@ struct bb_gemm_plan {
   int* status_dev = nullptr;
 };
 
-namespace {
+namespace bb {
+namespace gemm {
 
-int build_maps(bb::gemm::Plan& pl) {
+int build_maps(Plan& pl) {
   using namespace bb;
   const uint64_t M = pl.m, N = pl.n, K = pl.k, L = pl.l;
   {
@@ -50,6 +51,11 @@ int build_maps(bb::gemm::Plan& pl) {
   }
   return BB_OK;
 }
+
+}  // namespace gemm
+}  // namespace bb
+
+namespace {
 
 void fill_info(const bb::gemm::Plan& p, bb_gemm_info* info) {
   if (!info) return;
@@ -137,7 +143,7 @@ BB_API int bb_gemm_plan_create(int64_t m, int64_t n, int64_t k, int64_t l, const
     p.c_dtype = c_dtype;
     p.stream = static_cast<cudaStream_t>(stream);
     rc = gemm::plan_init(p, variant, dev.sm_count);
-    if (rc == BB_OK) rc = build_maps(p);
+    if (rc == BB_OK) rc = gemm::build_maps(p);
     if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
     if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
     if (rc == BB_OK && p.sk_parts > 0) {

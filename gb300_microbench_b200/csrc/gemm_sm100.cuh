@@ -39,5 +39,8 @@ struct Plan {
 // k, l, c_dtype set). Returns a BB_* status.
 int plan_init(Plan& pl, int variant, int sm_count);
 
+// Encodes the A, B and C tensor maps of a plan whose geometry is set.
+int build_maps(Plan& pl);
+
 }  // namespace gemm
 }  // namespace bb

@@ -119,6 +119,22 @@ BB_API int64_t bb_gemm_launches(const bb_gemm_plan* plan);
 /* Replaces p35_plan_destroy (cublaslt_bridge.cu:1008). */
 BB_API int bb_gemm_destroy(bb_gemm_plan* plan);
 
+/* GEMM for callers that cannot allocate device memory (code that runs where
+ * cudaMalloc is not allowed, such as inside an allocator's callbacks or a
+ * host that owns the whole device heap). No counterpart in the reference.
+ * Same kernel and results as the tuned variant of bb_gemm_plan_create /
+ * bb_gemm_execute, but no plan and no allocation: its scratch (the split-tail
+ * partial slices and counters, and the status word) is a static 16 MiB +
+ * 64 KiB device array that every GPU loading this library keeps until exit.
+ * Problems whose split tail needs more than 16 MiB of partial storage are
+ * rejected with BB_ERR_ARGUMENT. The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress), so make it before any stream
+ * capture. Calls share the array: calls that overlap on the GPU race. With
+ * wait != 0 the call synchronises `stream` and reports a device-side wait
+ * timeout as BB_ERR_TIMEOUT; with wait == 0 it only queues the work. */
+BB_API int bb_gemm_run_noalloc(int64_t m, int64_t n, int64_t k, int64_t l, const void* a, const void* b, void* c,
+                               int c_dtype, void* stream, int wait);
+
 /* ============================================================ copy kernels
  * HBM->SMEM streaming read of `bytes` from `src`, 1 CTA per SM. Replaces
  * ldgsts_validate_kernel / ldgsts_benchmark_kernel (memory_paths/ldgsts.cu:

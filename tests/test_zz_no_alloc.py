@@ -1,0 +1,79 @@
+"""The allocation-free GEMM entry point, bb_gemm_run_noalloc.
+
+Some callers cannot call cudaMalloc (an allocator's own callbacks, a plugin
+host that owns the whole device heap); this entry point serves them with the
+same tuned kernel, keeping its scratch in a static device array instead of
+a plan-owned allocation. This file checks, through the C ABI, that two calls
+in a row give the same C as the existing plan-based entry point
+(bb_gemm_plan_create + bb_gemm_execute) on the same inputs, including a
+shape whose split tail uses the static scratch. It is named to be collected
+last, and it passes alone in a fresh process as well as after the others.
+"""
+import ctypes
+
+import pytest
+import torch
+
+import oracle
+from gb300_microbench_b200 import _native as nat
+from gb300_microbench_b200 import inputs
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2  # relative Frobenius, the tolerance of the GEMM parity tests
+
+
+def _plan_result(a, b, c_dtype):
+    lib = nat.bench_lib()
+    m, k = a.shape
+    n = b.shape[0]
+    c = torch.full((m, n), float("nan"), dtype=c_dtype, device=a.device)
+    plan = ctypes.c_void_p()
+    info = nat.GemmInfo()
+    stream = torch.cuda.current_stream().cuda_stream
+    dt = nat.BB_DTYPE_BF16 if c_dtype == torch.bfloat16 else nat.BB_DTYPE_F32
+    nat.check("bb_gemm_plan_create", lib.bb_gemm_plan_create(
+        m, n, k, 1, a.data_ptr(), b.data_ptr(), c.data_ptr(), nat.BB_DTYPE_BF16, nat.BB_DTYPE_BF16, dt,
+        nat.BB_VARIANT_TUNED, stream, ctypes.byref(plan), ctypes.byref(info)))
+    nat.check("bb_gemm_execute", lib.bb_gemm_execute(plan))
+    nat.check("bb_gemm_synchronize", lib.bb_gemm_synchronize(plan))
+    lib.bb_gemm_destroy(plan)
+    return c
+
+
+def _noalloc_result(a, b, c_dtype):
+    lib = nat.bench_lib()
+    m, k = a.shape
+    n = b.shape[0]
+    c = torch.full((m, n), float("nan"), dtype=c_dtype, device=a.device)
+    dt = nat.BB_DTYPE_BF16 if c_dtype == torch.bfloat16 else nat.BB_DTYPE_F32
+    nat.check("bb_gemm_run_noalloc", lib.bb_gemm_run_noalloc(
+        m, n, k, 1, a.data_ptr(), b.data_ptr(), c.data_ptr(), dt, torch.cuda.current_stream().cuda_stream, 1))
+    return c
+
+
+@pytest.mark.parametrize("mnk,c_dtype", [((4096, 4096, 4096), torch.bfloat16),   # split tail: uses the scratch
+                                          ((32768, 512, 4096), torch.float32),    # split tail, FP32 C
+                                          ((1024, 768, 512), torch.bfloat16)])    # whole tiles only
+def test_noalloc_matches_plan_entry_point_twice(cuda_device, mnk, c_dtype):
+    m, n, k = mnk
+    a_cpu, b_cpu = inputs.baseline_mode_operands(m, n, k)
+    a, b = a_cpu.to(cuda_device), b_cpu.to(cuda_device)
+    want = _plan_result(a, b, c_dtype).float()
+    for _ in range(2):
+        got = _noalloc_result(a, b, c_dtype).float()
+        assert torch.isfinite(got).all()
+        err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+        assert err <= BF16_TOL, err
+        assert torch.equal(got, want)  # same kernel, fixed summation order
+    ref = oracle.gemm_reference_fp32(a_cpu[:256], b_cpu)
+    assert oracle.rel_frobenius(got[:256].cpu(), ref) <= BF16_TOL
+
+
+def test_noalloc_refuses_bad_arguments(cuda_device):
+    """Refused before anything is launched, with the reason in bb_last_error."""
+    lib = nat.bench_lib()
+    rc = lib.bb_gemm_run_noalloc(256, 256, 100, 1, None, None, None, nat.BB_DTYPE_BF16,
+                                 torch.cuda.current_stream().cuda_stream, 1)
+    assert rc == nat.BB_ERR_ARGUMENT
+    assert lib.bb_last_error()
