@@ -82,8 +82,8 @@ class GemmInfo(ctypes.Structure):
 class CopyInfo(ctypes.Structure):
     _fields_ = [(name, c_int64) for name in (
         "method", "stages", "bytes_in_flight_kib", "stage_bytes", "bytes_in_flight", "copies_per_thread",
-        "row_bytes", "tile_rows", "threads_per_cta", "grid_ctas", "smem_bytes", "total_tiles")] + [
-        ("reserved", c_int64 * 4)]
+        "row_bytes", "tile_rows", "threads_per_cta", "grid_ctas", "smem_bytes", "total_tiles",
+        "occupancy_ctas_per_sm")] + [("reserved", c_int64 * 3)]
 
     def as_dict(self) -> dict:
         return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}

@@ -92,24 +92,43 @@ int encode_tiled(CUtensorMap* out, CUtensorMapDataType dtype, int elem_bytes, in
 }
 
 int query_device(DeviceInfo* info) {
+  // cudaGetDeviceProperties costs milliseconds; properties are cached per
+  // device after the first query.
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool valid[64] = {};
   int dev = 0;
   BB_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (valid[dev]) {
+      *info = cache[dev];
+      return BB_OK;
+    }
+  }
   cudaDeviceProp prop{};
   BB_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
-  info->device = dev;
-  info->sm_count = prop.multiProcessorCount;
-  info->major = prop.major;
-  info->minor = prop.minor;
-  info->smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
-  info->l2_bytes = prop.l2CacheSize;
+  DeviceInfo d;
+  d.device = dev;
+  d.sm_count = prop.multiProcessorCount;
+  d.major = prop.major;
+  d.minor = prop.minor;
+  d.smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
+  d.l2_bytes = prop.l2CacheSize;
   int optin = 0;
   BB_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  info->smem_optin = optin;
+  d.smem_optin = optin;
   if (prop.major != 10 || prop.minor != 0) {
     set_error("device %d is compute capability %d.%d; this library is built for sm_100a (10.0) only", dev,
               prop.major, prop.minor);
     return BB_ERR_UNSUPPORTED;
   }
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    cache[dev] = d;
+    valid[dev] = true;
+  }
+  *info = d;
   return BB_OK;
 }
 

@@ -312,6 +312,7 @@ struct Geometry {
   int threads = 0;
   int smem = 0;
   int grid = 0;
+  int occupancy = 0;  // resident CTAs per SM of the benchmark kernel (0: not queried)
   int64_t total_tiles = 0;
 };
 
@@ -380,6 +381,19 @@ static int finish_geometry(Geometry* g, int* sm_count_out) {
 }
 
 template <typename K>
+static int occupancy_of(K kern, int threads, int smem, int* out) {
+  int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                      "cudaFuncSetAttribute(copy smem)");
+  if (rc != BB_OK) return rc;
+  return check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(out, kern, threads, smem),
+                    "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+}
+
+// Resident CTAs per SM of the benchmark kernel of this geometry (the
+// reference checks it is exactly 1: ldgsts.cu:821-835).
+static int query_occupancy(int method, Geometry* g);
+
+template <typename K>
 static int set_smem(K kern, int smem) {
   return check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                     "cudaFuncSetAttribute(copy smem)");
@@ -443,6 +457,22 @@ static int launch_tma(const Geometry& g, bool validate, const void* src, int64_t
   return BB_ERR_INTERNAL;
 }
 
+static int query_occupancy(int method, Geometry* g) {
+  if (method == BB_COPY_LDGSTS) {
+#define X(S, C) \
+  if (g->stages == S && g->copies == C) return occupancy_of(ldgsts_benchmark_kernel<S, C>, kLdgstsThreads, g->smem, &g->occupancy);
+    BB_LDGSTS_CASES(X)
+#undef X
+  } else {
+#define X(S) \
+  if (g->stages == S) return occupancy_of(tma_benchmark_kernel<S>, kTmaThreads, g->smem, &g->occupancy);
+    X(2) X(3) X(4) X(8)
+#undef X
+  }
+  set_error("copy: no specialisation for stages=%d", g->stages);
+  return BB_ERR_INTERNAL;
+}
+
 static int run(int method, int stages, int bif_kib, int row_bytes, const void* src, int64_t bytes, int64_t passes,
                int64_t rotation, bool validate, uint32_t* sink, unsigned long long* mism, int* status,
                void* stream) {
@@ -488,6 +518,8 @@ BB_API int bb_copy_plan(int method, int stages, int bif_kib, int row_bytes, int6
     if (sm_count <= 0) {
       rc = copy::finish_geometry(&g, nullptr);
       if (rc != BB_OK) return rc;
+      rc = copy::query_occupancy(method, &g);
+      if (rc != BB_OK) return rc;
     } else {
       g.smem = g.stages * g.stage_bytes;  // host-only estimate; the launch reserves > half an SM
     }
@@ -504,7 +536,8 @@ BB_API int bb_copy_plan(int method, int stages, int bif_kib, int row_bytes, int6
       info->grid_ctas = g.grid;
       info->smem_bytes = g.smem;
       info->total_tiles = g.total_tiles;
-      for (int i = 0; i < 4; ++i) info->reserved[i] = 0;
+      info->occupancy_ctas_per_sm = g.occupancy;
+      for (int i = 0; i < 3; ++i) info->reserved[i] = 0;
     }
     return BB_OK;
   } catch (...) {

@@ -162,7 +162,8 @@ typedef struct bb_copy_info {
   int64_t grid_ctas;
   int64_t smem_bytes;            /* dynamic shared memory reserved per CTA */
   int64_t total_tiles;
-  int64_t reserved[4];
+  int64_t occupancy_ctas_per_sm; /* benchmark kernel, 0 when not queried   */
+  int64_t reserved[3];
 } bb_copy_info;
 
 BB_API size_t bb_copy_info_size(void);
