@@ -120,15 +120,28 @@ BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_kernel_launches": (c_int64, []),
 }
 
+class CmpInfo(ctypes.Structure):
+    """bb_cmp_info of include/b200cmp.h."""
+    _fields_ = [(name, c_int64) for name in (
+        "layout", "cublaslt_version", "lda", "ldb", "ldc", "ldd", "transa", "transb", "order_a", "order_b",
+        "order_c", "order_d", "type_ab", "type_d", "compute_type", "scale_type", "pointer_mode", "epilogue",
+        "search_mode", "workspace_limit_bytes", "workspace_bytes", "heuristic_requested", "heuristic_returned",
+        "heuristic_index", "alignment_a_bytes", "alignment_b_bytes", "alignment_c_bytes", "alignment_d_bytes",
+        "algo_id", "tile_id", "stages_id", "split_k", "reduction_scheme", "cta_swizzling", "custom_option",
+        "inner_shape_id", "cluster_shape_id")] + [("waves_count", ctypes.c_double), ("alpha", ctypes.c_double),
+                                                   ("beta", ctypes.c_double)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 CMP_SIGNATURES: dict[str, tuple] = {
     "bb_cmp_abi_version": (c_int, []),
+    "bb_cmp_info_size": (c_size_t, []),
     "bb_cmp_last_error": (c_char_p, []),
-    "bb_cmp_plan_create": (c_int, [c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
-                                   POINTER(c_void_p)]),
+    "bb_cmp_plan_create": (c_int, [c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                   c_void_p, POINTER(c_void_p), POINTER(CmpInfo)]),
     "bb_cmp_execute_n": (c_int, [c_void_p, c_int]),
-    "bb_cmp_algo_index": (c_int, [c_void_p]),
-    "bb_cmp_algo_count": (c_int, [c_void_p]),
-    "bb_cmp_workspace_bytes": (c_int64, [c_void_p]),
     "bb_cmp_destroy": (c_int, [c_void_p]),
 }
 
@@ -181,8 +194,8 @@ def cmp_lib() -> ctypes.CDLL:
             _bind(lib, CMP_SIGNATURES)
         except (OSError, AttributeError) as exc:
             raise NativeLibraryError(f"cannot load {CMP_LIB_PATH}: {exc}") from exc
-        if lib.bb_cmp_abi_version() != 1:
-            raise NativeLibraryError("comparator ABI version mismatch")
+        if lib.bb_cmp_abi_version() != 2 or lib.bb_cmp_info_size() != ctypes.sizeof(CmpInfo):
+            raise NativeLibraryError("comparator ABI version or bb_cmp_info size mismatch")
         _cmp = lib
         return lib
 

@@ -45,6 +45,10 @@ def fixed6(x: float) -> str:
 
 
 def git_commit_hash() -> str:
+    """HEAD of this checkout; B200_GIT_COMMIT overrides it where the tree was
+    copied without .git (a launcher passes the commit it copied)."""
+    if os.environ.get("B200_GIT_COMMIT"):
+        return os.environ["B200_GIT_COMMIT"]
     try:
         out = subprocess.run(["git", "rev-parse", "HEAD"], cwd=REPO_ROOT, capture_output=True, text=True)
         return out.stdout.strip() if out.returncode == 0 and out.stdout.strip() else "UNKNOWN"
@@ -53,6 +57,8 @@ def git_commit_hash() -> str:
 
 
 def git_dirty_flag() -> str:
+    if os.environ.get("B200_GIT_DIRTY") in ("true", "false"):
+        return os.environ["B200_GIT_DIRTY"]
     try:
         out = subprocess.run(["git", "status", "--porcelain"], cwd=REPO_ROOT, capture_output=True, text=True)
         if out.returncode != 0:

@@ -1,12 +1,10 @@
 // cuBLASLt comparator (library GEMM) for the sm_100a GEMM of
-// libb200bench.so. Row-major D = A * B^T is expressed in cuBLASLt's
-// column-major terms as D^T (N x M) = B (N x K, col-major view K x N
-// transposed) * A^T: op(A_lt) = T on the K x N buffer of B, op(B_lt) = N on
-// the K x M buffer of A.
+// libb200bench.so; see include/b200cmp.h for the contract.
 #include <cublasLt.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstring>
 #include <new>
 #include <vector>
 
@@ -17,6 +15,21 @@ thread_local char g_err[512];
 void set_err(const char* what, int code) { std::snprintf(g_err, sizeof(g_err), "%s failed (status %d)", what, code); }
 constexpr size_t kWorkspaceLimit = 64ull << 20;
 constexpr int kHeuristics = 32;
+
+uint32_t alignment_of(const void* p) {
+  const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+  uint32_t a = 256;
+  while (a > 1 && (v % a) != 0) a >>= 1;
+  return a;
+}
+
+template <typename T>
+int64_t algo_attr(const cublasLtMatmulAlgo_t& algo, cublasLtMatmulAlgoConfigAttributes_t attr) {
+  T v{};
+  size_t written = 0;
+  if (cublasLtMatmulAlgoConfigGetAttribute(&algo, attr, &v, sizeof(v), &written) != CUBLAS_STATUS_SUCCESS) return -1;
+  return static_cast<int64_t>(v);
+}
 }  // namespace
 
 struct bb_cmp_plan {
@@ -24,11 +37,10 @@ struct bb_cmp_plan {
   cublasLtMatmulDesc_t op = nullptr;
   cublasLtMatrixLayout_t la = nullptr, lb = nullptr, ld = nullptr;
   cublasLtMatmulAlgo_t algo{};
-  int algo_index = -1, algo_count = 0;
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
-  const void* a = nullptr;
-  const void* b = nullptr;
+  const void* first = nullptr;   // cuBLASLt's "A" operand
+  const void* second = nullptr;  // cuBLASLt's "B" operand
   void* d = nullptr;
   cudaStream_t stream = nullptr;
   float alpha = 1.0f, beta = 0.0f;
@@ -55,7 +67,8 @@ struct bb_cmp_plan {
 
 extern "C" {
 
-BB_CMP_API int bb_cmp_abi_version(void) { return 1; }
+BB_CMP_API int bb_cmp_abi_version(void) { return 2; }
+BB_CMP_API size_t bb_cmp_info_size(void) { return sizeof(bb_cmp_info); }
 BB_CMP_API const char* bb_cmp_last_error(void) { return g_err; }
 
 BB_CMP_API int bb_cmp_destroy(bb_cmp_plan* p) {
@@ -71,36 +84,62 @@ BB_CMP_API int bb_cmp_destroy(bb_cmp_plan* p) {
 }
 
 BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
-                                  int d_dtype, int autotune, void* stream, bb_cmp_plan** out) {
+                                  int d_dtype, int layout, int autotune, void* stream, bb_cmp_plan** out,
+                                  bb_cmp_info* info) {
   try {
     g_err[0] = 0;
-    if (!out || m <= 0 || n <= 0 || k <= 0 || (d_dtype != 1 && d_dtype != 2)) {
+    if (!out || m <= 0 || n <= 0 || k <= 0 || (d_dtype != 1 && d_dtype != 2) ||
+        (layout != BB_CMP_LAYOUT_COLUMN && layout != BB_CMP_LAYOUT_REFERENCE)) {
       std::snprintf(g_err, sizeof(g_err), "bb_cmp_plan_create: bad argument");
       return 1;
     }
     *out = nullptr;
     bb_cmp_plan* p = new (std::nothrow) bb_cmp_plan();
     if (!p) return 6;
-    p->a = a;
-    p->b = b;
     p->d = d;
     p->stream = static_cast<cudaStream_t>(stream);
     const cudaDataType_t dt = d_dtype == 1 ? CUDA_R_16BF : CUDA_R_32F;
     LT(cublasLtCreate(&p->handle));
     LT(cublasLtMatmulDescCreate(&p->op, CUBLAS_COMPUTE_32F, CUDA_R_32F));
-    const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
+    cublasOperation_t tA, tB;
+    int64_t lda, ldb, ldd;
+    cublasLtOrder_t order = CUBLASLT_ORDER_COL;
+    if (layout == BB_CMP_LAYOUT_REFERENCE) {
+      // Row-major A (M x K), op N; row-major B (N x K), op T; row-major D.
+      tA = CUBLAS_OP_N;
+      tB = CUBLAS_OP_T;
+      p->first = a;
+      p->second = b;
+      lda = k;
+      ldb = k;
+      ldd = n;
+      order = CUBLASLT_ORDER_ROW;
+      LT(cublasLtMatrixLayoutCreate(&p->la, CUDA_R_16BF, m, k, lda));
+      LT(cublasLtMatrixLayoutCreate(&p->lb, CUDA_R_16BF, n, k, ldb));
+      LT(cublasLtMatrixLayoutCreate(&p->ld, dt, m, n, ldd));
+      for (cublasLtMatrixLayout_t l : {p->la, p->lb, p->ld}) {
+        LT(cublasLtMatrixLayoutSetAttribute(l, CUBLASLT_MATRIX_LAYOUT_ORDER, &order, sizeof(order)));
+      }
+    } else {
+      // D^T (N x M, col-major, ld N) = B (K x N col-major, ld K)^T * A^T (K x M col-major, ld K).
+      tA = CUBLAS_OP_T;
+      tB = CUBLAS_OP_N;
+      p->first = b;
+      p->second = a;
+      lda = k;
+      ldb = k;
+      ldd = n;
+      LT(cublasLtMatrixLayoutCreate(&p->la, CUDA_R_16BF, k, n, lda));
+      LT(cublasLtMatrixLayoutCreate(&p->lb, CUDA_R_16BF, k, m, ldb));
+      LT(cublasLtMatrixLayoutCreate(&p->ld, dt, n, m, ldd));
+    }
     LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA)));
     LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB)));
-    // "A" of cuBLASLt = our B buffer (K x N col-major, ld K), transposed.
-    LT(cublasLtMatrixLayoutCreate(&p->la, CUDA_R_16BF, k, n, k));
-    // "B" of cuBLASLt = our A buffer (K x M col-major, ld K).
-    LT(cublasLtMatrixLayoutCreate(&p->lb, CUDA_R_16BF, k, m, k));
-    // D^T: N x M col-major, ld N == our row-major M x N.
-    LT(cublasLtMatrixLayoutCreate(&p->ld, dt, n, m, n));
     cublasLtMatmulPreference_t pref = nullptr;
     LT(cublasLtMatmulPreferenceCreate(&pref));
     size_t ws = kWorkspaceLimit;
-    cublasStatus_t s = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws, sizeof(ws));
+    cublasStatus_t s =
+        cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws, sizeof(ws));
     std::vector<cublasLtMatmulHeuristicResult_t> res(kHeuristics);
     int found = 0;
     if (s == CUBLAS_STATUS_SUCCESS) {
@@ -113,7 +152,6 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
       bb_cmp_destroy(p);
       return 2;
     }
-    p->algo_count = found;
     size_t max_ws = 0;
     for (int i = 0; i < found; ++i)
       if (res[i].state == CUBLAS_STATUS_SUCCESS && res[i].workspaceSize > max_ws) max_ws = res[i].workspaceSize;
@@ -135,13 +173,13 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
         if (res[i].state != CUBLAS_STATUS_SUCCESS) continue;
         bool ok = true;
         for (int rep = 0; rep < 3 && ok; ++rep)
-          ok = cublasLtMatmul(p->handle, p->op, &p->alpha, p->b, p->la, p->a, p->lb, &p->beta, p->d, p->ld, p->d,
-                              p->ld, &res[i].algo, p->workspace, max_ws, p->stream) == CUBLAS_STATUS_SUCCESS;
+          ok = cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d, p->ld,
+                              p->d, p->ld, &res[i].algo, p->workspace, max_ws, p->stream) == CUBLAS_STATUS_SUCCESS;
         if (!ok) continue;
         cudaEventRecord(e0, p->stream);
         for (int rep = 0; rep < 5; ++rep)
-          cublasLtMatmul(p->handle, p->op, &p->alpha, p->b, p->la, p->a, p->lb, &p->beta, p->d, p->ld, p->d, p->ld,
-                         &res[i].algo, p->workspace, max_ws, p->stream);
+          cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d, p->ld, p->d,
+                         p->ld, &res[i].algo, p->workspace, max_ws, p->stream);
         cudaEventRecord(e1, p->stream);
         cudaEventSynchronize(e1);
         float ms = 0;
@@ -160,7 +198,46 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
       return 5;
     }
     p->algo = res[chosen].algo;
-    p->algo_index = chosen;
+    if (info) {
+      std::memset(info, 0, sizeof(*info));
+      info->layout = layout;
+      info->cublaslt_version = static_cast<int64_t>(cublasLtGetVersion());
+      info->lda = lda;
+      info->ldb = ldb;
+      info->ldc = ldd;
+      info->ldd = ldd;
+      info->transa = tA;
+      info->transb = tB;
+      info->order_a = info->order_b = info->order_c = info->order_d = order;
+      info->type_ab = CUDA_R_16BF;
+      info->type_d = dt;
+      info->compute_type = CUBLAS_COMPUTE_32F;
+      info->scale_type = CUDA_R_32F;
+      info->pointer_mode = CUBLASLT_POINTER_MODE_HOST;
+      info->epilogue = CUBLASLT_EPILOGUE_DEFAULT;
+      info->search_mode = CUBLASLT_SEARCH_BEST_FIT;
+      info->workspace_limit_bytes = static_cast<int64_t>(kWorkspaceLimit);
+      info->workspace_bytes = static_cast<int64_t>(max_ws);
+      info->heuristic_requested = kHeuristics;
+      info->heuristic_returned = found;
+      info->heuristic_index = chosen;
+      info->alignment_a_bytes = alignment_of(a);
+      info->alignment_b_bytes = alignment_of(b);
+      info->alignment_c_bytes = alignment_of(d);
+      info->alignment_d_bytes = alignment_of(d);
+      info->algo_id = algo_attr<int32_t>(p->algo, CUBLASLT_ALGO_CONFIG_ID);
+      info->tile_id = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_TILE_ID);
+      info->stages_id = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_STAGES_ID);
+      info->split_k = algo_attr<int32_t>(p->algo, CUBLASLT_ALGO_CONFIG_SPLITK_NUM);
+      info->reduction_scheme = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_REDUCTION_SCHEME);
+      info->cta_swizzling = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_CTA_SWIZZLING);
+      info->custom_option = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_CUSTOM_OPTION);
+      info->inner_shape_id = algo_attr<uint16_t>(p->algo, CUBLASLT_ALGO_CONFIG_INNER_SHAPE_ID);
+      info->cluster_shape_id = algo_attr<uint16_t>(p->algo, CUBLASLT_ALGO_CONFIG_CLUSTER_SHAPE_ID);
+      info->waves_count = res[chosen].wavesCount;
+      info->alpha = 1.0;
+      info->beta = 0.0;
+    }
     *out = p;
     return 0;
   } catch (...) {
@@ -172,8 +249,8 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
 BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* p, int iterations) {
   if (!p) return 1;
   for (int i = 0; i < iterations; ++i) {
-    cublasStatus_t s = cublasLtMatmul(p->handle, p->op, &p->alpha, p->b, p->la, p->a, p->lb, &p->beta, p->d, p->ld,
-                                      p->d, p->ld, &p->algo, p->workspace, p->workspace_bytes, p->stream);
+    cublasStatus_t s = cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d,
+                                      p->ld, p->d, p->ld, &p->algo, p->workspace, p->workspace_bytes, p->stream);
     if (s != CUBLAS_STATUS_SUCCESS) {
       set_err("cublasLtMatmul", static_cast<int>(s));
       return 2;
@@ -181,9 +258,5 @@ BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* p, int iterations) {
   }
   return 0;
 }
-
-BB_CMP_API int bb_cmp_algo_index(const bb_cmp_plan* p) { return p ? p->algo_index : -1; }
-BB_CMP_API int bb_cmp_algo_count(const bb_cmp_plan* p) { return p ? p->algo_count : -1; }
-BB_CMP_API int64_t bb_cmp_workspace_bytes(const bb_cmp_plan* p) { return p ? static_cast<int64_t>(p->workspace_bytes) : -1; }
 
 }  // extern "C"

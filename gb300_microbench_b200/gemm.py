@@ -131,10 +131,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.bfloat
 
 
 class CublasLtPlan:
-    """The cuBLASLt comparator on the same tensors (library call)."""
+    """The cuBLASLt comparator on the same tensors (a library call, the
+    role of the reference's cublaslt_bridge.cu). ``layout="reference"`` uses
+    the reference's row-major descriptor (cublaslt_bridge.cu:75-128),
+    ``"column"`` the column-major view."""
+
+    LAYOUTS = {"column": 0, "reference": 1}
 
     def __init__(self, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, autotune: bool = False,
-                 stream: torch.cuda.Stream | None = None):
+                 stream: torch.cuda.Stream | None = None, layout: str = "column"):
         if a.dim() != 2:
             raise ValueError("the comparator takes 2-D operands")
         self._lib = nat.cmp_lib()
@@ -142,14 +147,17 @@ class CublasLtPlan:
         m, k = a.shape
         n = b.shape[0]
         handle = ctypes.c_void_p()
+        info = nat.CmpInfo()
         rc = self._lib.bb_cmp_plan_create(m, n, k, a.data_ptr(), b.data_ptr(), c.data_ptr(), _DTYPES[c.dtype],
-                                          1 if autotune else 0, self.stream.cuda_stream, ctypes.byref(handle))
+                                          self.LAYOUTS[layout], 1 if autotune else 0, self.stream.cuda_stream,
+                                          ctypes.byref(handle), ctypes.byref(info))
         if rc != 0:
             raise nat.NativeCallError("bb_cmp_plan_create", rc, self._lib.bb_cmp_last_error().decode())
         self._handle = handle
-        self.algo_index = int(self._lib.bb_cmp_algo_index(handle))
-        self.algo_count = int(self._lib.bb_cmp_algo_count(handle))
-        self.workspace_bytes = int(self._lib.bb_cmp_workspace_bytes(handle))
+        self.info = info.as_dict()
+        self.algo_index = int(info.heuristic_index)
+        self.algo_count = int(info.heuristic_returned)
+        self.workspace_bytes = int(info.workspace_bytes)
 
     def run(self, iterations: int = 1) -> None:
         rc = self._lib.bb_cmp_execute_n(self._handle, int(iterations))

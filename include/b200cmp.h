@@ -5,11 +5,18 @@
  * (gemm_comparison/cublaslt_bridge.cu) for BF16 A/B with either FP32 D (the
  * reference's frozen descriptor, cublaslt_bridge.cu:75-128) or BF16 D.
  *
- * Layout contract: A (M,K) row-major BF16, B (N,K) row-major BF16,
- * D (M,N) row-major; D = A * B^T, FP32 compute, alpha = 1, beta = 0.
- * Algorithm policy as in the reference (cublaslt_bridge.cu:40-53): up to
- * 32 heuristic results with a 64 MiB workspace limit, the first supported
- * one is used unless bb_cmp_plan_create is asked to autotune.
+ * Problem: D = A * B^T, A (M,K) row-major BF16, B (N,K) row-major BF16,
+ * D (M,N) row-major, FP32 compute and scale, alpha = 1, beta = 0.
+ * Two descriptor layouts give the same result:
+ *   BB_CMP_LAYOUT_REFERENCE  the reference's descriptor: CUBLASLT_ORDER_ROW
+ *                            on all four matrices, TRANSA = N, TRANSB = T
+ *                            (cublaslt_bridge.cu:75-128);
+ *   BB_CMP_LAYOUT_COLUMN     the column-major view D^T = B * A^T
+ *                            (TRANSA = T, TRANSB = N, default order).
+ * Algorithm policy as in the reference (cublaslt_bridge.cu:40-53): 32
+ * heuristic results requested with a 64 MiB workspace limit, best-fit
+ * search, the first supported one used, unless autotune is asked for (every
+ * supported result timed once, the fastest kept).
  */
 #ifndef B200CMP_H_
 #define B200CMP_H_
@@ -23,19 +30,37 @@ extern "C" {
 
 #define BB_CMP_API __attribute__((visibility("default")))
 
+enum { BB_CMP_LAYOUT_COLUMN = 0, BB_CMP_LAYOUT_REFERENCE = 1 };
+
+/* Plan metadata, 8-byte fields (the cuBLASLt columns of the reference's
+ * CSV, gemm_comparison.py:344-381, and P35PlanInfo, cublaslt_bridge.cu:
+ * 156-220). Enum-valued fields hold the cuBLASLt enum values. */
+typedef struct bb_cmp_info {
+  int64_t layout;
+  int64_t cublaslt_version;
+  int64_t lda, ldb, ldc, ldd;
+  int64_t transa, transb;
+  int64_t order_a, order_b, order_c, order_d;
+  int64_t type_ab, type_d, compute_type, scale_type, pointer_mode, epilogue, search_mode;
+  int64_t workspace_limit_bytes, workspace_bytes;
+  int64_t heuristic_requested, heuristic_returned, heuristic_index;
+  int64_t alignment_a_bytes, alignment_b_bytes, alignment_c_bytes, alignment_d_bytes;
+  int64_t algo_id, tile_id, stages_id, split_k, reduction_scheme, cta_swizzling, custom_option,
+      inner_shape_id, cluster_shape_id;
+  double waves_count;
+  double alpha, beta;
+} bb_cmp_info;
+
 typedef struct bb_cmp_plan bb_cmp_plan;
 
 BB_CMP_API int bb_cmp_abi_version(void);
+BB_CMP_API size_t bb_cmp_info_size(void);
 BB_CMP_API const char* bb_cmp_last_error(void);
-/* d_dtype: 1 = BF16, 2 = FP32 (same codes as BB_DTYPE_*). autotune != 0
- * times every returned heuristic once and keeps the fastest. */
+/* d_dtype: 1 = BF16, 2 = FP32 (BB_DTYPE_* of b200bench.h). */
 BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a, const void* b, void* d,
-                                  int d_dtype, int autotune, void* stream, bb_cmp_plan** plan);
+                                  int d_dtype, int layout, int autotune, void* stream, bb_cmp_plan** plan,
+                                  bb_cmp_info* info);
 BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* plan, int iterations);
-/* Index of the heuristic result in use and the number returned. */
-BB_CMP_API int bb_cmp_algo_index(const bb_cmp_plan* plan);
-BB_CMP_API int bb_cmp_algo_count(const bb_cmp_plan* plan);
-BB_CMP_API int64_t bb_cmp_workspace_bytes(const bb_cmp_plan* plan);
 BB_CMP_API int bb_cmp_destroy(bb_cmp_plan* plan);
 
 #ifdef __cplusplus

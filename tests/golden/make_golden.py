@@ -41,6 +41,34 @@ def pattern_py(i: int) -> list[int]:
     return [lo & 0xFFFFFFFF, lo >> 32, hi & 0xFFFFFFFF, hi >> 32]
 
 
+def write_csv_headers(reference: Path) -> None:
+    """csv_headers.json: the reference's three raw CSV schemas, read from its
+    sources (memory_paths/ldgsts.cu:734-745, umma_throughput/umma_1sm.cu:
+    965-973, gemm_comparison/gemm_comparison.py:319-429)."""
+    import importlib.util
+    import re
+
+    def header_from_cu(path: Path) -> list[str]:
+        text = path.read_text()
+        block = text[text.index("void print_csv_header()"):]
+        block = block[: block.index("}")]
+        return "".join(re.findall(r'"([^"]*)"', block)).replace("\\n", "").strip().split(",")
+
+    spec = importlib.util.spec_from_file_location("ref_gemm_comparison",
+                                                  reference / "gemm_comparison" / "gemm_comparison.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    (HERE / "csv_headers.json").write_text(json.dumps({
+        "source": "print_csv_header of memory_paths/ldgsts.cu, memory_paths/tma.cu, umma_throughput/umma_1sm.cu, "
+                  "umma_throughput/umma_2sm.cu; CSV_FIELDS of gemm_comparison/gemm_comparison.py",
+        "memory_paths": header_from_cu(reference / "memory_paths" / "ldgsts.cu"),
+        "memory_paths_tma": header_from_cu(reference / "memory_paths" / "tma.cu"),
+        "umma": header_from_cu(reference / "umma_throughput" / "umma_1sm.cu"),
+        "umma_2sm": header_from_cu(reference / "umma_throughput" / "umma_2sm.cu"),
+        "gemm": list(mod.CSV_FIELDS),
+    }, indent=1) + "\n")
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -82,6 +110,7 @@ def main() -> int:
     (HERE / "pattern.json").write_text(json.dumps({
         "source": "SplitMix64 pattern of memory_paths/ldgsts.cu:220-232, pure-Python restatement",
         "vectors": vectors}, indent=1) + "\n")
+    write_csv_headers(Path(args.reference))
     print("golden fixtures written", file=sys.stderr)
     return 0
 

@@ -47,7 +47,8 @@ def test_abi_handshake(libs):
     assert bench.bb_abi_version() == nat.ABI_VERSION
     assert bench.bb_gemm_info_size() == ctypes.sizeof(nat.GemmInfo) == 16 * 8
     assert bench.bb_copy_info_size() == ctypes.sizeof(nat.CopyInfo)
-    assert cmp.bb_cmp_abi_version() == 1
+    assert cmp.bb_cmp_abi_version() == 2
+    assert cmp.bb_cmp_info_size() == ctypes.sizeof(nat.CmpInfo)
     assert bench.bb_status_name(nat.BB_ERR_TIMEOUT) == b"TIMEOUT"
 
 
