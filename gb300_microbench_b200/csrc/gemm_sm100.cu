@@ -117,14 +117,22 @@ template <int kCG, int kBN, bool kOutF32>
 struct Cfg {
   static constexpr int BM = 128;              // accumulator rows held by one CTA
   static constexpr int TILE_M = BM * kCG;     // rows of one cluster tile
-  static constexpr int B_ROWS = kBN / kCG;    // B rows staged by one CTA
+  // One MMA instruction covers at most N = 256 columns; a 512-wide tile is
+  // two N = 256 MMAs per K step that share the A operand.
+  static constexpr int MMA_N = kBN > 256 ? 256 : kBN;
+  static constexpr int N_SUB = kBN / MMA_N;
+  static constexpr int B_BOX_ROWS = MMA_N / kCG;  // B rows of one CTA for one MMA (one TMA box)
+  static constexpr int B_SUB_BYTES = B_BOX_ROWS * kBK * 2;
   static constexpr int A_BYTES = BM * kBK * 2;
-  static constexpr int B_BYTES = B_ROWS * kBK * 2;
+  static constexpr int B_BYTES = N_SUB * B_SUB_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_COLS = kOutF32 ? 32 : 64;  // C columns per 128-byte store row
   static constexpr int EPI_BOX_BYTES = 32 * 128;      // 32 rows x 128 bytes
   static constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
-  static constexpr int TMEM_COLS = 2 * kBN;
+  // Two accumulator buffers (epilogue of tile i overlaps the MMAs of tile
+  // i+1) when they fit in the 512 TMEM columns, else one.
+  static constexpr int ACC_BUFS = 2 * kBN <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = ACC_BUFS * kBN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in maximum per block
   static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
@@ -137,7 +145,7 @@ struct Cfg {
   static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
   // MMA shape legality for kind::f16: M=128 needs N%16==0, 16<=N<=256;
   // M=256 (cta_group::2) the same.
-  static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "UMMA N");
+  static_assert(MMA_N % 16 == 0 && MMA_N >= 16 && MMA_N <= 256 && kBN % MMA_N == 0, "UMMA N");
 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& l, int& m_blk, int& n_blk) {
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int l, m_blk, n_blk;
         tile_coords(p, it.tile, l, m_blk, n_blk);
         const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM;
-        const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_ROWS;
+        const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_BOX_ROWS;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
             ok = false;
@@ -246,10 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kCG == 2) {
             const uint32_t fbc = mapa_shared(fb, full_target_rank);
             tma_load_3d_pair(da, &tm_a, fbc, kb * kBK, a_row, l);
-            tma_load_3d_pair(db, &tm_b, fbc, kb * kBK, b_row, l);
+#pragma unroll
+            for (int h = 0; h < C::N_SUB; ++h)
+              tma_load_3d_pair(db + h * C::B_SUB_BYTES, &tm_b, fbc, kb * kBK, b_row + h * C::MMA_N, l);
           } else {
             tma_load_3d(da, &tm_a, fb, kb * kBK, a_row, l);
-            tma_load_3d(db, &tm_b, fb, kb * kBK, b_row, l);
+#pragma unroll
+            for (int h = 0; h < C::N_SUB; ++h)
+              tma_load_3d(db + h * C::B_SUB_BYTES, &tm_b, fb, kb * kBK, b_row + h * C::MMA_N, l);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -275,15 +287,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (mma_cta && lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(C::TILE_M, kBN);
+      constexpr uint32_t idesc = make_idesc_bf16_f32(C::TILE_M, C::MMA_N);
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_iter = 0;
       WorkItem it;
       for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx, ++acc_iter) {
-        const uint32_t acc = acc_iter & 1u;
-        const uint32_t acc_phase = (acc_iter >> 1) & 1u;
+        const uint32_t acc = acc_iter % C::ACC_BUFS;
+        const uint32_t acc_phase = (acc_iter / C::ACC_BUFS) & 1u;
         if (!bb_wait<kCG == 2>(smem_u32(&tmem_empty[acc]), acc_phase ^ 1u, p.status, kDevTimeoutMma)) {
           ok = false;
           break;
@@ -300,8 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_f16<kCG>(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32),
-                          idesc, (kb != it.kb0 || kk != 0) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < C::N_SUB; ++h) {
+              umma_f16<kCG>(d_tmem + h * C::MMA_N, sw128_kmajor_desc(a_addr + kk * 32),
+                            sw128_kmajor_desc(b_addr + h * C::B_SUB_BYTES + kk * 32), idesc,
+                            (kb != it.kb0 || kk != 0) ? 1u : 0u);
+            }
           }
           const uint32_t eb = smem_u32(&empty[stage]);
           umma_commit<kCG>(eb);
@@ -378,8 +394,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int idx = 0; next_item(p, cluster_idx, idx, it); ++idx, ++acc_iter) {
       int l, m_blk, n_blk;
       tile_coords(p, it.tile, l, m_blk, n_blk);
-      const uint32_t acc = acc_iter & 1u;
-      const uint32_t acc_phase = (acc_iter >> 1) & 1u;
+      const uint32_t acc = acc_iter % C::ACC_BUFS;
+      const uint32_t acc_phase = (acc_iter / C::ACC_BUFS) & 1u;
       if (!bb_wait<kCG == 2>(smem_u32(&tmem_full[acc]), acc_phase, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const int row0 = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
@@ -421,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int parts = p.sk_parts;
         const int j = it.part;
         const int row = q * 32 + lane;
-        const int slice = kBN / parts;  // multiple of 64: parts in {2, 4}, kBN 128 or 256
+        const int slice = kBN / parts;  // multiple of 64: parts in {2, 4}, kBN 128, 256 or 512
         // Block (i, w): part w's values of column slice i (w != i), BM rows x
         // slice columns; the tile's (parts - 1) * parts blocks are packed.
         const int64_t tile_base = (static_cast<int64_t>(t_local) * kCG + rank) * (parts - 1) * (C::BM * kBN);
@@ -544,11 +560,33 @@ static KernelChoice choose(int variant, int64_t m, int64_t n, int64_t k, int sm_
     case BB_VARIANT_PERSISTENT_2CTA: return {2, 128, true, 8, false};
     default: break;
   }
-  (void)k;
-  (void)sm_count;
-  // Tuned: 256 x 256 pair tiles everywhere they fill the machine.
-  if (n >= 256 && m >= 256) return {2, 256, true, 8, true};
-  return {1, 128, true, 8, true};
+  // Tuned: CTA-pair tiles wherever they fill the machine.
+  if (n < 256 || m < 256) return {1, 128, true, 8, true};
+  // Two CTA-pair tile shapes: 256 x 256 (double-buffered TMEM accumulator,
+  // split tail) and 256 x 512 (two N = 256 MMAs per K step sharing A: 36 %
+  // fewer operand bytes staged per FLOP, but one accumulator buffer, so
+  // each tile's epilogue is exposed). BB_GEMM_TILE_N=256|512 forces one.
+  const char* tn = std::getenv("BB_GEMM_TILE_N");
+  if (tn && std::atoi(tn) == 256) return {2, 256, true, 8, true};
+  if (tn && std::atoi(tn) == 512) return {2, 512, true, 8, true};
+  const int P = sm_count / 2;
+  const double kb = static_cast<double>((k + kBK - 1) / kBK);
+  auto tiles = [&](int tn_) { return ((m + 255) / 256) * ((n + tn_ - 1) / tn_); };
+  // Modelled time in units of one 256 x 256 tile at full tensor rate; the
+  // per-shape efficiencies are the measured main-loop tensor-pipe activity.
+  const int64_t t256 = tiles(256);
+  const int64_t full = t256 / P, rem = t256 % P;
+  double tail = 0.0;
+  if (rem) {
+    int sp = static_cast<int>(P / rem);
+    sp = sp > 4 ? 4 : (sp == 3 ? 2 : sp);
+    const bool split = kb >= 48 && sp >= 2 && static_cast<double>(t256) / ((full + 1.0) * P) < 0.95;
+    tail = split ? 1.0 / sp + 16.0 / kb : 1.0;
+  }
+  const double time256 = (full + tail) / 0.87;
+  const int64_t t512 = tiles(512);
+  const double time512 = static_cast<double>((t512 + P - 1) / P) * 2.0 / 0.96 * (1.0 + 2.0 / kb);
+  return time512 < time256 ? KernelChoice{2, 512, true, 8, true} : KernelChoice{2, 256, true, 8, true};
 }
 
 template <int kCG, int kBN, bool kOutF32>
@@ -601,7 +639,7 @@ static int prepare(Plan& pl, int sm_count) {
   pl.stages = C::STAGES;
   pl.smem_bytes = C::SMEM_BYTES;
   pl.tmem_cols = C::TMEM_COLS;
-  pl.b_rows = C::B_ROWS;
+  pl.b_rows = C::B_BOX_ROWS;
   pl.epi_cols = C::EPI_COLS;
   pl.tiles_m = static_cast<int>((pl.m + C::TILE_M - 1) / C::TILE_M);
   pl.tiles_n = static_cast<int>((pl.n + kBN - 1) / kBN);
@@ -684,6 +722,7 @@ int plan_init(Plan& pl, int variant, int sm_count) {
   else if (ch.cg == 1 && ch.bn == 256) rc = f32 ? prepare<1, 256, true>(pl, sm_count) : prepare<1, 256, false>(pl, sm_count);
   else if (ch.cg == 2 && ch.bn == 128) rc = f32 ? prepare<2, 128, true>(pl, sm_count) : prepare<2, 128, false>(pl, sm_count);
   else if (ch.cg == 2 && ch.bn == 256) rc = f32 ? prepare<2, 256, true>(pl, sm_count) : prepare<2, 256, false>(pl, sm_count);
+  else if (ch.cg == 2 && ch.bn == 512) rc = f32 ? prepare<2, 512, true>(pl, sm_count) : prepare<2, 512, false>(pl, sm_count);
   if (rc == BB_ERR_INTERNAL) set_error("no kernel for cta_group=%d bn=%d", ch.cg, ch.bn);
   return rc;
 }

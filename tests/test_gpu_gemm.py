@@ -167,3 +167,26 @@ def test_split_tail_deterministic_bf16(cuda_device):
         assert torch.equal(first, c)
     ref = oracle.gemm_reference_fp32(a, b)
     assert oracle.rel_frobenius(c.cpu().float(), ref) <= BF16_TOL
+
+
+@pytest.mark.parametrize("tile_n", ["256", "512"])
+@pytest.mark.parametrize("mnk,force_split", [((512, 1024, 512), False), ((300, 600, 200), False),
+                                             ((1024, 1536, 4096), True), ((4096, 4096, 3072), True),
+                                             ((8192, 512, 1024), False)])
+def test_tuned_tile_shapes_exact(cuda_device, monkeypatch, tile_n, mnk, force_split):
+    """Both CTA-pair tile shapes of the tuned variant (256 x 256 with a
+    double-buffered accumulator, 256 x 512 with two N = 256 MMAs per K step),
+    including ragged N (half of the second MMA outside C) and the split
+    tail, are exact on integer operands."""
+    monkeypatch.setenv("BB_GEMM_TILE_N", tile_n)
+    if force_split:
+        monkeypatch.setenv("BB_GEMM_STREAM_K", "1")
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    for out in (torch.float32, torch.bfloat16):
+        c = _run(a[0], b[0], out, "tuned", cuda_device)
+        ref = oracle.gemm_reference_fp32(a[0], b[0])
+        if out == torch.float32:
+            assert torch.equal(c, ref)
+        else:
+            assert torch.equal(c, ref.to(torch.bfloat16))
