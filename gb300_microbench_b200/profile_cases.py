@@ -1,0 +1,67 @@
+"""Small, self-contained programs to run under a profiler: one case of one
+kernel, a few launches, nothing else.
+
+    python -m gb300_microbench_b200.profile_cases gemm M N K VARIANT [out_dtype]
+    python -m gb300_microbench_b200.profile_cases copy METHOD STAGES BIF_KIB ROW_BYTES MIB
+    python -m gb300_microbench_b200.profile_cases umma CTA_GROUP N DEPTH ITERATIONS
+
+gemm: N(0,1) BF16 operands (torch.Generator seed 0), 4 launches of the plan.
+copy: a MIB-MiB seeded uniform-u32 buffer, 3 one-pass launches.
+umma: the reference's integer operands, 2 launches.
+Each prints "ok" and exits 0 when the kernel reported no device error.
+"""
+from __future__ import annotations
+
+import sys
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    import torch
+
+    if not argv:
+        print(__doc__)
+        return 2
+    what, args = argv[0], argv[1:]
+    if what == "gemm":
+        from .gemm import GemmPlan
+
+        m, n, k = (int(x) for x in args[:3])
+        variant = args[3] if len(args) > 3 else "tuned"
+        out = torch.float32 if len(args) > 4 and args[4] == "f32" else torch.bfloat16
+        g = torch.Generator().manual_seed(0)
+        a = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+        b = torch.randn(n, k, generator=g).to(torch.bfloat16).cuda()
+        c = torch.empty(m, n, dtype=out, device="cuda")
+        plan = GemmPlan(a, b, c, variant=variant)
+        plan.run(4)
+        plan.synchronize()
+    elif what == "copy":
+        from . import streaming
+
+        method, stages, bif, row_bytes, mib = args[0], int(args[1]), int(args[2]), int(args[3]), int(args[4])
+        buf = torch.empty(mib * 1024 * 1024 // 4, dtype=torch.int32, device="cuda")
+        streaming.fill_uniform_u32(buf)
+        run = streaming.StreamingRun(method, stages, bif, buf, row_bytes=row_bytes)
+        for _ in range(3):
+            run.run()
+        run.checksums()
+        run.check_status()
+    elif what == "umma":
+        from . import inputs, umma
+
+        cg, n, depth, iters = (int(x) for x in args[:4])
+        a, b = inputs.umma_pattern_operands(cg, n)
+        probe = umma.UmmaProbe(cg, n, depth, a.cuda(), b.cuda())
+        for _ in range(2):
+            probe.launch(iters)
+        probe.result()
+    else:
+        print(__doc__)
+        return 2
+    print("ok")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
