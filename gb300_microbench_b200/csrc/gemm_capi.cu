@@ -70,7 +70,7 @@ void fill_info(const bb::gemm::Plan& p, bb_gemm_info* info) {
   info->num_tiles = p.num_tiles;
   info->smem_bytes = p.smem_bytes;
   info->tmem_columns = p.tmem_cols;
-  info->threads_per_cta = 192;
+  info->threads_per_cta = p.threads;
   info->persistent = p.persistent ? 1 : 0;
   info->raster_group_m = p.group_m;
   info->c_dtype = p.c_dtype;

@@ -110,7 +110,6 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-constexpr int kThreads = 192;
 constexpr int kBK = 64;  // K elements per stage: one 128-byte swizzle row of BF16
 
 template <int kCG, int kBN, bool kOutF32>
@@ -128,7 +127,15 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_COLS = kOutF32 ? 32 : 64;  // C columns per 128-byte store row
   static constexpr int EPI_BOX_BYTES = 32 * 128;      // 32 rows x 128 bytes
-  static constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
+  // A 512-wide accumulator is drained by eight epilogue warps (two per TMEM
+  // lane quarter, each owning half the columns) so the single accumulator
+  // buffer goes back to the MMA sooner; narrower tiles use four.
+  static constexpr int EPI_WARPS = kBN > 256 ? 8 : 4;
+  static constexpr int EPI_COL_SPLIT = EPI_WARPS / 4;
+  static constexpr int WARP_COLS = kBN / EPI_COL_SPLIT;
+  static constexpr int EPI_BUFS = EPI_WARPS == 8 ? 1 : 2;  // staging boxes per warp
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_BOX_BYTES;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   // Two accumulator buffers (epilogue of tile i overlaps the MMAs of tile
   // i+1) when they fit in the 512 TMEM columns, else one.
   static constexpr int ACC_BUFS = 2 * kBN <= 512 ? 2 : 1;
@@ -162,7 +169,7 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& l, int&
 }
 
 template <int kCG, int kBN, bool kOutF32>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
     bb_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_c, const Params p) {
   using C = Cfg<kCG, kBN, kOutF32>;
@@ -170,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Launch contract, checked before any barrier, TMEM or cluster operation.
   const uint32_t rank = (kCG == 2) ? cluster_ctarank() : 0u;
-  if (blockDim.x != kThreads || (kCG == 2 && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
+  if (blockDim.x != C::THREADS || (kCG == 2 && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
     if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kDevBadLaunch);
     return;
   }
@@ -205,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tmem_full[a]), 1);
-      mbar_init(smem_u32(&tmem_empty[a]), 4 * kCG);
+      mbar_init(smem_u32(&tmem_empty[a]), C::EPI_WARPS * kCG);
     }
     mbar_init(smem_u32(mma_done), 1);
     fence_mbarrier_init_cluster();
@@ -339,19 +346,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int ep_tid = threadIdx.x - 64;  // 0..127 within the epilogue warpgroup
-    uint8_t* ebuf = smem_epi + (warp - 2) * 2 * C::EPI_BOX_BYTES;
+    const int ep_tid = threadIdx.x - 64;  // index within the epilogue warps
+    constexpr int kEpiThreads = C::EPI_WARPS * 32;
+    const int wc0 = ((warp - 2) / 4) * C::WARP_COLS;  // this warp's columns: [wc0, wc0 + WARP_COLS)
+    uint8_t* ebuf = smem_epi + (warp - 2) * C::EPI_BUFS * C::EPI_BOX_BYTES;
     const uint32_t ebuf_u32 = smem_u32(ebuf);
     uint32_t acc_iter = 0;
     int chunk_seq = 0;
-    constexpr int kChunks = kBN / C::EPI_COLS;
 
     // Stages one 32-row x 128-byte chunk in swizzled shared memory and
     // stores it to C with TMA.
     auto store_chunk = [&](const uint32_t (&packed)[32], int row0, int col0, int l) {
-      const uint32_t buf = ebuf_u32 + (chunk_seq & 1) * C::EPI_BOX_BYTES;
+      const uint32_t buf = ebuf_u32 + (chunk_seq % C::EPI_BUFS) * C::EPI_BOX_BYTES;
       ++chunk_seq;
-      if (lane == 0) bulk_wait_group_read<1>();
+      if (lane == 0) bulk_wait_group_read<C::EPI_BUFS - 1>();
       __syncwarp();
       const uint32_t row_addr = buf + lane * 128;
 #pragma unroll
@@ -403,27 +411,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int ncols = kOutF32 ? 32 : 64;  // accumulator columns behind one 128-byte store row
 
       if (it.part < 0) {
-        // ---- whole tile: TMEM -> registers -> C
-#pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          float v[64];
-          uint32_t r0[32];
-          tmem_ld_32x32b_x32(t_row + c * ncols, r0);
-          if constexpr (!kOutF32) {
-            uint32_t r1[32];
-            tmem_ld_32x32b_x32(t_row + c * ncols + 32, r1);
+        if constexpr (!kOutF32 && C::EPI_COL_SPLIT == 2) {
+          // ---- whole 512-wide tile, BF16: the warp's 256 columns are
+          // converted into registers (128 packed words), the accumulator is
+          // released, and only then staged and stored.
+          uint32_t pk[C::WARP_COLS / 64][32];
+#pragma unroll
+          for (int h = 0; h < C::WARP_COLS / 32; ++h) {
+            uint32_t r0[32];
+            tmem_ld_32x32b_x32(t_row + wc0 + h * 32, r0);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(r1[j]);
-          } else {
-            tmem_ld_wait();
+            for (int jj = 0; jj < 16; ++jj)
+              pk[h / 2][(h & 1) * 16 + jj] = pack_bf16x2(__uint_as_float(r0[2 * jj]), __uint_as_float(r0[2 * jj + 1]));
           }
+          release_acc(acc);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
-          if (c == kChunks - 1) release_acc(acc);  // accumulator now lives in registers
-          uint32_t packed[32];
-          pack_chunk(v, packed);
-          store_chunk(packed, row0, n_blk * kBN + c * C::EPI_COLS, l);
+          for (int cc = 0; cc < C::WARP_COLS / 64; ++cc) store_chunk(pk[cc], row0, n_blk * kBN + wc0 + cc * 64, l);
+        } else {
+          // ---- whole tile: TMEM -> registers -> C, one store row at a time
+          constexpr int kWarpChunks = C::WARP_COLS / C::EPI_COLS;
+#pragma unroll 1
+          for (int c = 0; c < kWarpChunks; ++c) {
+            const int col = wc0 + c * ncols;
+            float v[64];
+            uint32_t r0[32];
+            tmem_ld_32x32b_x32(t_row + col, r0);
+            if constexpr (!kOutF32) {
+              uint32_t r1[32];
+              tmem_ld_32x32b_x32(t_row + col + 32, r1);
+              tmem_ld_wait();
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) v[32 + jj] = __uint_as_float(r1[jj]);
+            } else {
+              tmem_ld_wait();
+            }
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] = __uint_as_float(r0[jj]);
+            if (c == kWarpChunks - 1) release_acc(acc);  // accumulator now lives in registers
+            uint32_t packed[32];
+            pack_chunk(v, packed);
+            store_chunk(packed, row0, n_blk * kBN + col, l);
+          }
         }
       } else {
         // ---- part j of a tile split in s along K. Columns are cut into s
@@ -446,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           return reinterpret_cast<float4*>(p.partials + tile_base + static_cast<int64_t>(idx) * C::BM * slice) + row;
         };
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = wc0 / 32; c < (wc0 + C::WARP_COLS) / 32; ++c) {
           const int i = (c * 32) / slice;
           if (i == j) continue;  // own slice stays in TMEM
           float4* dst = block_ptr(i, j) + ((c * 32 - i * slice) / 4) * C::BM;
@@ -461,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __threadfence();
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         int* arrived = p.counters + 2 * (t_local * kCG + static_cast<int>(rank));
         int* done = arrived + 1;
         if (ep_tid == 0) {
@@ -469,11 +498,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_flag[0] = spin_until_at_least(arrived, parts, p.status, kDevTimeoutEpilogue) ? 1 : 0;
           __threadfence();
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         const bool peers_ok = epi_flag[0] != 0;
         if (peers_ok) {
 #pragma unroll 1
-          for (int c = j * slice / ncols; c < (j + 1) * slice / ncols; ++c) {
+          const int own0 = j * slice > wc0 ? j * slice : wc0;
+          const int own1 = (j + 1) * slice < wc0 + C::WARP_COLS ? (j + 1) * slice : wc0 + C::WARP_COLS;
+          for (int c = own0 / ncols; c < own1 / ncols; ++c) {
             float own[64];
             {
               uint32_t r0[32];
@@ -517,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         release_acc(acc);
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         if (ep_tid == 0 && peers_ok) {
           // Every part has passed its wait: the last one resets both
           // counters for the next launch.
@@ -595,7 +626,7 @@ static int launch(const Plan& pl) {
   auto kern = bb_gemm_kernel<kCG, kBN, kOutF32>;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.grid), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = pl.stream;
   cudaLaunchAttribute attr[2];
@@ -636,6 +667,7 @@ static int prepare(Plan& pl, int sm_count) {
   }
   pl.tile_m = C::TILE_M;
   pl.tile_n = kBN;
+  pl.threads = C::THREADS;
   pl.stages = C::STAGES;
   pl.smem_bytes = C::SMEM_BYTES;
   pl.tmem_cols = C::TMEM_COLS;
@@ -650,7 +682,7 @@ static int prepare(Plan& pl, int sm_count) {
   {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(kCG * max_clusters), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(C::THREADS, 1, 1);
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

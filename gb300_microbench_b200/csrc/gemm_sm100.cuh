@@ -19,6 +19,7 @@ struct Plan {
   int variant = 0;
   cudaStream_t stream = nullptr;
   CUtensorMap tm_a{}, tm_b{}, tm_c{};
+  int threads = 0;
   int cg = 1, tile_m = 0, tile_n = 0, stages = 0, smem_bytes = 0, tmem_cols = 0, b_rows = 0, epi_cols = 0;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, k_blocks = 0, group_m = 8, max_active_clusters = 0, grid = 0;
   bool persistent = true;
