@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_int, c_int64, c_size_t, c_uint32, c_uint64, c_ulonglong, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_uint64, c_ulonglong, c_void_p
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"
@@ -89,6 +89,19 @@ class CopyInfo(ctypes.Structure):
         return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
 
 
+class LowpInfo(ctypes.Structure):
+    """bb_lowp_info of include/b200bench.h."""
+    _fields_ = [(name, c_int64) for name in (
+        "kind", "tile_m", "tile_n", "tile_k", "stages", "grid_ctas", "num_tiles", "smem_bytes", "tmem_columns",
+        "threads_per_cta")] + [("reserved", c_int64 * 6)]
+
+    def as_dict(self) -> dict:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
+
+
+BB_LOWP_NVFP4 = 1
+BB_LOWP_FP8_BLOCK128 = 2
+
 # Every symbol include/b200bench.h declares, with (restype, argtypes).
 BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_abi_version": (c_int, []),
@@ -118,6 +131,14 @@ BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_umma_kernel_name": (c_char_p, [c_int, c_int, c_int]),
     "bb_test_wait_timeout": (c_int, [c_int64, c_void_p, c_void_p]),
     "bb_kernel_launches": (c_int64, []),
+    "bb_lowp_info_size": (c_size_t, []),
+    "bb_lowp_scale_bytes": (c_int64, [c_int, c_int64, c_int64]),
+    "bb_lowp_plan_create": (c_int, [c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_float, c_void_p, c_void_p, POINTER(c_void_p), POINTER(LowpInfo)]),
+    "bb_lowp_execute_n": (c_int, [c_void_p, c_int]),
+    "bb_lowp_synchronize": (c_int, [c_void_p]),
+    "bb_lowp_launches": (c_int64, [c_void_p]),
+    "bb_lowp_destroy": (c_int, [c_void_p]),
 }
 
 class CmpInfo(ctypes.Structure):
@@ -177,6 +198,8 @@ def bench_lib() -> ctypes.CDLL:
             raise NativeLibraryError("bb_gemm_info size mismatch")
         if lib.bb_copy_info_size() != ctypes.sizeof(CopyInfo):
             raise NativeLibraryError("bb_copy_info size mismatch")
+        if lib.bb_lowp_info_size() != ctypes.sizeof(LowpInfo):
+            raise NativeLibraryError("bb_lowp_info size mismatch")
         _bench = lib
         return lib
 

@@ -29,7 +29,15 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                      "-I", str(INCLUDE), "--expt-relaxed-constexpr"]
 
-BENCH_SOURCES = ["common.cu", "gemm_sm100.cu", "gemm_capi.cu", "gemm_noalloc.cu", "copy_kernels.cu", "umma_probe.cu"]
+BENCH_SOURCES = [
+    "common.cu",
+    "gemm_sm100.cu",
+    "gemm_capi.cu",
+    "gemm_noalloc.cu",
+    "gemm_lowp.cu",
+    "copy_kernels.cu",
+    "umma_probe.cu",
+]
 CMP_SOURCES = ["cublaslt_cmp.cu"]
 
 BENCH_LIB = LIB / "libb200bench.so"

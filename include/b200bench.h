@@ -228,6 +228,53 @@ BB_API int bb_test_wait_timeout(int64_t budget_ns, int* status, void* stream);
 /* Library-wide count of kernels launched through this ABI. */
 BB_API int64_t bb_kernel_launches(void);
 
+/* ====================================================== block-scaled GEMM
+ * D (M x N, BF16, row-major) = dequant(A) * dequant(B)^T, FP32 accumulate.
+ * The reference has no low-precision GEMM; this is its dense GEMM plan
+ * interface (bb_gemm_plan_create above, after cublaslt_bridge.cu:563)
+ * extended with the two scale operands.
+ *
+ * BB_LOWP_NVFP4: A (M x K/2 bytes) and B (N x K/2 bytes) hold E2M1 values,
+ *   two per byte, element 2i in the low nibble. sfa / sfb hold one UE4M3
+ *   scale per 16 K elements as 512-byte atoms: for 128-row block rb and
+ *   64-wide K group kg, atom (rb * K/64 + kg); scale j of row r inside it at
+ *   byte (r % 32) * 16 + (r / 32) * 4 + j (rows past M / N are padding).
+ *   global_scale is the product of the two per-tensor FP32 scales.
+ *   K must be a multiple of 256.
+ * BB_LOWP_FP8_BLOCK128: A (M x K) and B (N x K) hold E4M3 bytes. sfa is
+ *   FP32 [ceil(M/128)][K/128] and sfb FP32 [ceil(N/128)][K/128], one scale
+ *   per 128 x 128 block; global_scale multiplies the result (1 for none).
+ *   K must be a multiple of 128.
+ * N must be a multiple of 8 and every buffer 16-byte aligned. */
+enum { BB_LOWP_NVFP4 = 1, BB_LOWP_FP8_BLOCK128 = 2 };
+
+typedef struct bb_lowp_info {
+  int64_t kind;
+  int64_t tile_m, tile_n, tile_k; /* output tile and K elements per stage */
+  int64_t stages;
+  int64_t grid_ctas;
+  int64_t num_tiles;
+  int64_t smem_bytes;
+  int64_t tmem_columns;
+  int64_t threads_per_cta;
+  int64_t reserved[6];
+} bb_lowp_info;
+
+typedef struct bb_lowp_plan bb_lowp_plan;
+
+BB_API size_t bb_lowp_info_size(void);
+/* Bytes of one scale operand (sfa with rows = M, sfb with rows = N), or -1
+ * when K does not fit the kind. */
+BB_API int64_t bb_lowp_scale_bytes(int kind, int64_t rows, int64_t k);
+BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                               const void* sfa, const void* sfb, float global_scale, void* d, void* stream,
+                               bb_lowp_plan** plan, bb_lowp_info* info);
+BB_API int bb_lowp_execute_n(bb_lowp_plan* plan, int iterations);
+/* Waits for the plan's stream; BB_ERR_TIMEOUT if a device wait ran out. */
+BB_API int bb_lowp_synchronize(bb_lowp_plan* plan);
+BB_API int64_t bb_lowp_launches(const bb_lowp_plan* plan);
+BB_API int bb_lowp_destroy(bb_lowp_plan* plan);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,133 @@
+"""Block-scaled GEMM parity on the GPU through the C ABI.
+
+Two kinds of cases per format:
+* exact: operands encoded directly with power-of-two block scales and small
+  values, so every product and partial sum is exact in FP32; D must equal the
+  oracle's FP32 result rounded to BF16 bit for bit. These pin the operand,
+  scale-atom and TMEM scale layouts.
+* quantised N(0, 1): relative Frobenius error of D against the FP32 matmul of
+  the dequantised inputs <= 2e-2 (the configuration's check); observed errors
+  are BF16 output rounding, about 2e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle import lowp as olp
+from gb300_microbench_b200 import lowp
+
+pytestmark = pytest.mark.gpu
+
+LOWP_TOL = 2e-2  # relative Frobenius
+
+
+def _e4m3_pow2(exps: torch.Tensor) -> torch.Tensor:
+    """E4M3 bits of 2^e for -6 <= e <= 8."""
+    return ((exps + 7) << 3).to(torch.uint8)
+
+
+def _nvfp4_exact_operand(rows, k, gen):
+    codes = torch.randint(0, 16, (rows, k), generator=gen, dtype=torch.uint8)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    exps = torch.randint(-1, 2, (rows, k // 16), generator=gen)
+    return lowp.Nvfp4Operand.from_parts(packed, _e4m3_pow2(exps), 1.0)
+
+
+def _fp8_exact_operand(rows, k, gen):
+    # E4M3 integers 0..15 with random sign: exactly representable.
+    ints = torch.randint(0, 16, (rows, k), generator=gen).float()
+    sign = torch.where(torch.rand(rows, k, generator=gen) < 0.5, -1.0, 1.0)
+    q = (ints * sign).to(torch.float8_e4m3fn).view(torch.uint8)
+    exps = torch.randint(-1, 2, (-(-rows // 128), k // 128), generator=gen)
+    return lowp.Fp8BlockOperand.from_parts(q, torch.exp2(exps.float()))
+
+
+def _oracle_d(kind, a, b):
+    if kind == "nvfp4":
+        ad = olp.nvfp4_dequant(a.data.cpu().numpy(), a.atoms.cpu().numpy(), a.tensor_scale, a.rows, a.k)
+        bd = olp.nvfp4_dequant(b.data.cpu().numpy(), b.atoms.cpu().numpy(), b.tensor_scale, b.rows, b.k)
+    else:
+        ad = olp.fp8_block_dequant(a.data.cpu().numpy(), a.scales.cpu().numpy())
+        bd = olp.fp8_block_dequant(b.data.cpu().numpy(), b.scales.cpu().numpy())
+    return olp.gemm_dequant_fp32(ad, bd)
+
+
+def _run(kind, a, b, dev):
+    ad, bd = a.to(dev), b.to(dev)
+    d = torch.full((a.rows, b.rows), float("nan"), dtype=torch.bfloat16, device=dev)
+    plan = lowp.LowpGemmPlan(kind, ad, bd, d)
+    plan.run()
+    plan.synchronize()
+    assert plan.launches == 1
+    plan.close()
+    return d.cpu()
+
+
+EXACT_SHAPES = [(128, 256, 256), (256, 512, 512), (384, 256, 1024), (200, 264, 512), (1024, 768, 768)]
+
+
+@pytest.mark.parametrize("kind", ["nvfp4", "fp8_block128"])
+@pytest.mark.parametrize("mnk", EXACT_SHAPES)
+def test_exact(cuda_device, kind, mnk):
+    m, n, k = mnk
+    if kind == "nvfp4" and k % 256:
+        pytest.skip("NVFP4 needs K % 256 == 0")
+    gen = torch.Generator().manual_seed(m * 7 + n * 3 + k)
+    make = _nvfp4_exact_operand if kind == "nvfp4" else _fp8_exact_operand
+    a, b = make(m, k, gen), make(n, k, gen)
+    ref = _oracle_d(kind, a, b)
+    d = _run(kind, a, b, cuda_device)
+    ref_bf16 = torch.from_numpy(ref).to(torch.bfloat16)
+    mismatch = (d.view(torch.int16) != ref_bf16.view(torch.int16)).sum().item()
+    assert mismatch == 0, f"{mismatch} of {m * n} elements differ from the exact result"
+
+
+@pytest.mark.parametrize("kind", ["nvfp4", "fp8_block128"])
+@pytest.mark.parametrize("mnk", [(256, 256, 512), (512, 1024, 2048), (1000, 776, 1536)])
+def test_quantised_normal(cuda_device, kind, mnk):
+    m, n, k = mnk
+    x, y = lowp.config4_inputs(m, n, k, seed=0, device="cpu")
+    op = lowp.Nvfp4Operand if kind == "nvfp4" else lowp.Fp8BlockOperand
+    a, b = op(x), op(y)
+    ref = _oracle_d(kind, a, b)
+    d = _run(kind, a, b, cuda_device).float().numpy()
+    err = oracle.rel_frobenius(torch.from_numpy(d), torch.from_numpy(ref))
+    assert err <= LOWP_TOL, err
+    assert err <= 5e-3, f"error {err} well above BF16 output rounding"
+
+
+def test_argument_errors(cuda_device):
+    gen = torch.Generator().manual_seed(0)
+    a = _nvfp4_exact_operand(128, 256, gen).to(cuda_device)
+    b = _nvfp4_exact_operand(256, 256, gen).to(cuda_device)
+    with pytest.raises(ValueError):
+        lowp.LowpGemmPlan("nvfp4", a, b, torch.empty(128, 255, dtype=torch.bfloat16, device=cuda_device))
+    from gb300_microbench_b200 import _native as nat
+    with pytest.raises(nat.NativeCallError):
+        # K = 128 is not a multiple of the NVFP4 stage (256)
+        a2 = _nvfp4_exact_operand(128, 128, gen).to(cuda_device)
+        b2 = _nvfp4_exact_operand(256, 128, gen).to(cuda_device)
+        lowp.LowpGemmPlan("nvfp4", a2, b2, torch.empty(128, 256, dtype=torch.bfloat16, device=cuda_device))
+
+
+def test_config4_size_checksums(cuda_device):
+    """Full 8192^3 size: D of the quantised N(0, 1) inputs against the
+    dequantised FP32 product on a sampled set of rows (the full FP32 oracle
+    at this size is minutes of CPU)."""
+    m = n = k = 8192
+    x, y = lowp.config4_inputs(m, n, k, seed=0, device=cuda_device)
+    for kind, op in (("nvfp4", lowp.Nvfp4Operand), ("fp8_block128", lowp.Fp8BlockOperand)):
+        a, b = op(x), op(y)
+        d = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_device)
+        plan = lowp.LowpGemmPlan(kind, a, b, d)
+        plan.run()
+        plan.synchronize()
+        rows = torch.arange(0, m, 61, device=cuda_device)
+        ad = a.dequantize()[rows].double()
+        bd = b.dequantize().double()
+        ref = (ad @ bd.T)
+        err = ((d[rows].double() - ref).norm() / ref.norm()).item()
+        assert err <= LOWP_TOL, (kind, err)
+        plan.close()
+        del a, b, d
