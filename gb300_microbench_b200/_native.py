@@ -93,7 +93,7 @@ class LowpInfo(ctypes.Structure):
     """bb_lowp_info of include/b200bench.h."""
     _fields_ = [(name, c_int64) for name in (
         "kind", "tile_m", "tile_n", "tile_k", "stages", "grid_ctas", "num_tiles", "smem_bytes", "tmem_columns",
-        "threads_per_cta")] + [("reserved", c_int64 * 6)]
+        "threads_per_cta", "cta_group")] + [("reserved", c_int64 * 5)]
 
     def as_dict(self) -> dict:
         return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
@@ -162,6 +162,8 @@ CMP_SIGNATURES: dict[str, tuple] = {
     "bb_cmp_last_error": (c_char_p, []),
     "bb_cmp_plan_create": (c_int, [c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                    c_void_p, POINTER(c_void_p), POINTER(CmpInfo)]),
+    "bb_cmp_lowp_plan_create": (c_int, [c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_float, c_void_p, c_int, c_void_p, POINTER(c_void_p), POINTER(CmpInfo)]),
     "bb_cmp_execute_n": (c_int, [c_void_p, c_int]),
     "bb_cmp_destroy": (c_int, [c_void_p]),
 }

@@ -246,6 +246,151 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
   }
 }
 
+BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const void* a, const void* b,
+                                       const void* sfa, const void* sfb, float global_scale, void* d, int autotune,
+                                       void* stream, bb_cmp_plan** out, bb_cmp_info* info) {
+  try {
+    g_err[0] = 0;
+    if (!out || m <= 0 || n <= 0 || k <= 0 || (kind != 1 && kind != 2) || !a || !b || !sfa || !sfb || !d) {
+      std::snprintf(g_err, sizeof(g_err), "bb_cmp_lowp_plan_create: bad argument");
+      return 1;
+    }
+    *out = nullptr;
+    bb_cmp_plan* p = new (std::nothrow) bb_cmp_plan();
+    if (!p) return 6;
+    p->d = d;
+    p->stream = static_cast<cudaStream_t>(stream);
+    p->alpha = global_scale;
+    const cudaDataType_t tab = kind == 1 ? CUDA_R_4F_E2M1 : CUDA_R_8F_E4M3;
+    const cublasLtMatmulMatrixScale_t mode =
+        kind == 1 ? CUBLASLT_MATMUL_MATRIX_SCALE_VEC16_UE4M3 : CUBLASLT_MATMUL_MATRIX_SCALE_BLK128x128_32F;
+    LT(cublasLtCreate(&p->handle));
+    LT(cublasLtMatmulDescCreate(&p->op, CUBLAS_COMPUTE_32F, CUDA_R_32F));
+    // Column-major view (the only one the narrow types allow, "TN"):
+    // D^T (N x M, ld N) = B (K x N, ld K)^T * A (K x M, ld K); cuBLASLt's A is
+    // our B with B's scales, its B is our A with A's scales.
+    const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
+    p->first = b;
+    p->second = a;
+    LT(cublasLtMatrixLayoutCreate(&p->la, tab, k, n, k));
+    LT(cublasLtMatrixLayoutCreate(&p->lb, tab, k, m, k));
+    LT(cublasLtMatrixLayoutCreate(&p->ld, CUDA_R_16BF, n, m, n));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA)));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB)));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_MODE, &mode, sizeof(mode)));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_MODE, &mode, sizeof(mode)));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_POINTER, &sfb, sizeof(sfb)));
+    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_POINTER, &sfa, sizeof(sfa)));
+    cublasLtMatmulPreference_t pref = nullptr;
+    LT(cublasLtMatmulPreferenceCreate(&pref));
+    size_t ws = kWorkspaceLimit;
+    cublasStatus_t s =
+        cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws, sizeof(ws));
+    std::vector<cublasLtMatmulHeuristicResult_t> res(kHeuristics);
+    int found = 0;
+    if (s == CUBLAS_STATUS_SUCCESS) {
+      s = cublasLtMatmulAlgoGetHeuristic(p->handle, p->op, p->la, p->lb, p->ld, p->ld, pref, kHeuristics, res.data(),
+                                         &found);
+    }
+    cublasLtMatmulPreferenceDestroy(pref);
+    if (s != CUBLAS_STATUS_SUCCESS || found == 0) {
+      std::snprintf(g_err, sizeof(g_err), "cuBLASLt %d offers no algorithm for this block-scaled GEMM (status %d)",
+                    static_cast<int>(cublasLtGetVersion()), static_cast<int>(s));
+      bb_cmp_destroy(p);
+      return 5;
+    }
+    size_t max_ws = 0;
+    for (int i = 0; i < found; ++i)
+      if (res[i].state == CUBLAS_STATUS_SUCCESS && res[i].workspaceSize > max_ws) max_ws = res[i].workspaceSize;
+    if (max_ws > 0) CU(cudaMalloc(&p->workspace, max_ws));
+    p->workspace_bytes = max_ws;
+    int chosen = -1;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (autotune) {
+      CU(cudaEventCreate(&e0));
+      CU(cudaEventCreate(&e1));
+    }
+    float best = 1e30f;
+    for (int i = 0; i < found; ++i) {
+      if (res[i].state != CUBLAS_STATUS_SUCCESS) continue;
+      if (!autotune) {
+        chosen = i;
+        break;
+      }
+      bool ok = true;
+      for (int rep = 0; rep < 3 && ok; ++rep)
+        ok = cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d, p->ld,
+                            p->d, p->ld, &res[i].algo, p->workspace, max_ws, p->stream) == CUBLAS_STATUS_SUCCESS;
+      if (!ok) continue;
+      cudaEventRecord(e0, p->stream);
+      for (int rep = 0; rep < 5; ++rep)
+        cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d, p->ld, p->d,
+                       p->ld, &res[i].algo, p->workspace, max_ws, p->stream);
+      cudaEventRecord(e1, p->stream);
+      cudaEventSynchronize(e1);
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e0, e1);
+      if (ms < best) {
+        best = ms;
+        chosen = i;
+      }
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (chosen < 0) {
+      std::snprintf(g_err, sizeof(g_err), "no supported cuBLASLt algorithm");
+      bb_cmp_destroy(p);
+      return 5;
+    }
+    p->algo = res[chosen].algo;
+    if (info) {
+      std::memset(info, 0, sizeof(*info));
+      info->layout = BB_CMP_LAYOUT_COLUMN;
+      info->cublaslt_version = static_cast<int64_t>(cublasLtGetVersion());
+      info->lda = k;
+      info->ldb = k;
+      info->ldc = n;
+      info->ldd = n;
+      info->transa = tA;
+      info->transb = tB;
+      info->order_a = info->order_b = info->order_c = info->order_d = CUBLASLT_ORDER_COL;
+      info->type_ab = tab;
+      info->type_d = CUDA_R_16BF;
+      info->compute_type = CUBLAS_COMPUTE_32F;
+      info->scale_type = CUDA_R_32F;
+      info->pointer_mode = CUBLASLT_POINTER_MODE_HOST;
+      info->epilogue = CUBLASLT_EPILOGUE_DEFAULT;
+      info->search_mode = CUBLASLT_SEARCH_BEST_FIT;
+      info->workspace_limit_bytes = static_cast<int64_t>(kWorkspaceLimit);
+      info->workspace_bytes = static_cast<int64_t>(max_ws);
+      info->heuristic_requested = kHeuristics;
+      info->heuristic_returned = found;
+      info->heuristic_index = chosen;
+      info->alignment_a_bytes = alignment_of(b);
+      info->alignment_b_bytes = alignment_of(a);
+      info->alignment_c_bytes = alignment_of(d);
+      info->alignment_d_bytes = alignment_of(d);
+      info->algo_id = algo_attr<int32_t>(p->algo, CUBLASLT_ALGO_CONFIG_ID);
+      info->tile_id = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_TILE_ID);
+      info->stages_id = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_STAGES_ID);
+      info->split_k = algo_attr<int32_t>(p->algo, CUBLASLT_ALGO_CONFIG_SPLITK_NUM);
+      info->reduction_scheme = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_REDUCTION_SCHEME);
+      info->cta_swizzling = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_CTA_SWIZZLING);
+      info->custom_option = algo_attr<uint32_t>(p->algo, CUBLASLT_ALGO_CONFIG_CUSTOM_OPTION);
+      info->inner_shape_id = algo_attr<uint16_t>(p->algo, CUBLASLT_ALGO_CONFIG_INNER_SHAPE_ID);
+      info->cluster_shape_id = algo_attr<uint16_t>(p->algo, CUBLASLT_ALGO_CONFIG_CLUSTER_SHAPE_ID);
+      info->waves_count = res[chosen].wavesCount;
+      info->alpha = global_scale;
+      info->beta = 0.0;
+    }
+    *out = p;
+    return 0;
+  } catch (...) {
+    std::snprintf(g_err, sizeof(g_err), "bb_cmp_lowp_plan_create: exception");
+    return 6;
+  }
+}
+
 BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* p, int iterations) {
   if (!p) return 1;
   for (int i = 0; i < iterations; ++i) {

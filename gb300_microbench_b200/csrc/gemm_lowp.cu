@@ -19,9 +19,14 @@
 //          warps into FP32 registers: acc += partial * sa[m][kb] * sb[n][kb].
 //          The MMA of K block kb+1 overlaps the promotion of kb.
 //
-// Roles (320 threads, one CTA per SM, 128 x 256 output tile per CTA):
-//   warp 0      producer: TMA loads of A (128 x 128 B) and B (256 x 128 B)
-//               per K block, plus (NVFP4) bulk copies of the scale atoms.
+// Tiles: 128 x 256 per CTA, or 256 x 256 per CTA pair (tcgen05.mma
+// .cta_group::2; each CTA stages its own 128 A rows and 128 of the B rows,
+// loads complete on the leader CTA's barriers, the leader's single thread
+// issues the scale copies and MMAs and commits to both CTAs' barriers).
+// Roles (320 threads, one CTA per SM):
+//   warp 0      producer: TMA loads of A (128 x 128 B) and B (256 or 128 x
+//               128 B) per K block, plus (NVFP4) the scale atoms (one 2 KiB
+//               box for A's 128-row block, one 4 KiB box for B's 256 rows).
 //   warp 1      TMEM allocation (512 columns) and the single MMA thread.
 //   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column
 //               half (w - 2) / 4, converts to BF16 and stores D directly.
@@ -32,6 +37,7 @@
 #include <cuda_bf16.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <new>
 
 #include "common.cuh"
@@ -44,29 +50,42 @@ namespace lowp {
 
 enum Kind : int { kNvfp4 = BB_LOWP_NVFP4, kFp8Block = BB_LOWP_FP8_BLOCK128 };
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int ROW_BYTES = 128;               // K bytes of one stage row (one swizzle row)
-constexpr int A_BYTES = BM * ROW_BYTES;      // 16 KiB
-constexpr int B_BYTES = BN * ROW_BYTES;      // 32 KiB
-constexpr int SFA_BYTES = 4 * 512;           // NVFP4: 4 atoms (256 K) x 1 row block
-constexpr int SFB_BYTES = 2 * 4 * 512;       // NVFP4: 4 atoms x 2 row blocks
-constexpr int STAGES = 4;
+constexpr int BM = 128;         // accumulator rows per CTA
+constexpr int ROW_BYTES = 128;  // K bytes of one stage row (one 128-byte swizzle row)
+constexpr int SF_ATOM = 512;    // bytes of one scale atom (128 rows x 4 scales)
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr int BAR_BYTES = 256;
 constexpr int GROUP_M = 8;
+constexpr int SMEM_LIMIT = 232448;
 
-template <int kKind>
+// kCG = 1: one CTA computes a 128 x 256 tile. kCG = 2: a CTA pair computes a
+// 256 x 256 tile with tcgen05.mma.cta_group::2; each CTA stages its own 128
+// rows of A and 128 of the 256 B rows, its own A scale atoms and all 256 rows
+// of B scale atoms (each CTA's TMEM needs the scales of every B row).
+template <int kKind, int kCG>
 struct Cfg {
+  static constexpr int TILE_M = BM * kCG;
+  static constexpr int TILE_N = 256;
+  static constexpr int B_ROWS = TILE_N / kCG;                      // B rows staged per CTA
   static constexpr int K_PER_STAGE = kKind == kNvfp4 ? 256 : 128;  // elements
   static constexpr int MMA_K = kKind == kNvfp4 ? 64 : 32;          // elements per instruction
   static constexpr int MMAS = K_PER_STAGE / MMA_K;                 // 4
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + (kKind == kNvfp4 ? SFA_BYTES + SFB_BYTES : 0);
+  static constexpr int A_BYTES = BM * ROW_BYTES;
+  static constexpr int B_BYTES = B_ROWS * ROW_BYTES;
+  static constexpr int SFA_BYTES = kKind == kNvfp4 ? MMAS * SF_ATOM : 0;      // one row block
+  static constexpr int SFB_BYTES = kKind == kNvfp4 ? 2 * MMAS * SF_ATOM : 0;  // two row blocks
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES) / STAGE_BYTES;
+  // NVFP4 keeps one TMEM scale area (48 columns) per stage next to the
+  // 256-column accumulator.
+  static constexpr int STAGES_MAX = kKind == kNvfp4 ? 5 : 8;
+  static constexpr int STAGES = STAGES_FIT < STAGES_MAX ? STAGES_FIT : STAGES_MAX;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
-  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
   static_assert(MMAS * 32 == ROW_BYTES, "one instruction consumes 32 bytes of each row");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
 };
 
 // NVFP4 TMEM map: accumulator columns [0, 256); per stage s a scale area at
@@ -74,15 +93,16 @@ struct Cfg {
 // (8 columns: two 128-row atoms). FP8 TMEM map: partial buffer b at 256 b.
 constexpr uint32_t kSfBase = 256;
 constexpr uint32_t kSfStageCols = 48;
-static_assert(kSfBase + STAGES * kSfStageCols <= TMEM_COLS, "TMEM scale ring");
+static_assert(kSfBase + Cfg<kNvfp4, 1>::STAGES * kSfStageCols <= TMEM_COLS, "TMEM scale ring");
+static_assert(kSfBase + Cfg<kNvfp4, 2>::STAGES * kSfStageCols <= TMEM_COLS, "TMEM scale ring");
 
 struct Params {
   int32_t m, n, k;
   int32_t tiles_m, tiles_n, num_tiles;
   int32_t k_stages;    // K / K_PER_STAGE
-  int32_t k_groups;    // NVFP4: K / 64 (atoms per row block)
-  int32_t rb_n;        // NVFP4: 128-row blocks of B's scales
-  const uint8_t* sfa;  // NVFP4 atoms, or FP8 FP32 block scales (as bytes)
+  int32_t rb_m, rb_n;  // 128-row blocks of A and B
+  int32_t num_clusters;
+  const uint8_t* sfa;  // FP8: FP32 block scales (NVFP4 scales travel by TMA)
   const uint8_t* sfb;
   float global_scale;
   __nv_bfloat16* d;
@@ -104,40 +124,79 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
 }
 static_assert(idesc_f8(128, 256) == 0x08400010u, "f8f6f4 idesc");
 static_assert(idesc_nvf4(128, 256) == 0x08400480u, "mxf4nvf4 idesc");
+static_assert(idesc_nvf4(256, 256) == 0x10400480u, "mxf4nvf4 idesc, CTA pair");
 
+template <int kCG>
 __device__ __forceinline__ void mma_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
+  if constexpr (kCG == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+  }
 }
+template <int kCG>
 __device__ __forceinline__ void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t tsfa,
                                          uint32_t tsfb, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
-          d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
-      : "memory");
+  if constexpr (kCG == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+        : "memory");
+  }
 }
-// One 512-byte scale atom (32 rows x 16 bytes) from shared memory into 4
-// TMEM columns, replicated into the four 32-lane quarters.
-__device__ __forceinline__ void tmem_cp_atom(uint32_t taddr, uint32_t smem_addr) {
-  // Interleaved (no-swizzle) K-major layout: 8-row core matrices of 128
-  // contiguous bytes, stacked every 128 bytes along the rows (SBO).
-  const uint64_t desc = make_smem_desc(smem_addr, 128, 128, kLayoutNone);
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+// Shared-memory descriptor of one 512-byte scale atom (32 rows x 16 bytes):
+// interleaved (no-swizzle) K-major layout, 8-row core matrices of 128
+// contiguous bytes stacked every 128 bytes along the rows (SBO).
+__device__ __forceinline__ uint64_t sf_atom_desc(uint32_t smem_addr) {
+  return make_smem_desc(smem_addr, 128, 128, kLayoutNone);
 }
-// Non-tensor bulk copy global -> this CTA's shared memory, completing on an
-// mbarrier of this CTA.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(mbar)
-      : "memory");
+// One scale atom into 4 TMEM columns, replicated into the four 32-lane
+// quarters (each quarter of the MMA reads its own lanes). With cta_group::2
+// each CTA of the pair copies from its own shared memory into its own TMEM.
+template <int kCG>
+__device__ __forceinline__ void tmem_cp_desc(uint32_t taddr, uint64_t desc) {
+  if constexpr (kCG == 1) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+  } else {
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+  }
+}
+
+// Rank-2 tile loads: into this CTA's shared memory, completing on this CTA's
+// mbarrier (1 CTA) or on the leader CTA's mbarrier (pair form). The data goes
+// to the issuing CTA only.
+template <int kCG>
+__device__ __forceinline__ void load_2d(uint32_t dst, const void* tmap, uint32_t mbar, int32_t x, int32_t y) {
+  if constexpr (kCG == 1) {
+    tma_load_2d(dst, tmap, mbar, x, y);
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(tmap), "r"(mbar), "r"(x), "r"(y)
+        : "memory");
+  }
 }
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& m_blk, int& n_blk) {
@@ -178,35 +237,58 @@ __device__ __forceinline__ void store_row(const Params& p, int row, int col0, co
   }
 }
 
-template <int kKind>
+// FP32 promotion acc += v * s for 32 values, two lanes per instruction
+// (packed fma.rn.f32x2 of sm_100).
+__device__ __forceinline__ void promote32(float* acc, const uint32_t (&v)[32], float s) {
+  const uint64_t s2 = (static_cast<uint64_t>(__float_as_uint(s)) << 32) | __float_as_uint(s);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uint64_t a2 = (static_cast<uint64_t>(__float_as_uint(acc[2 * j + 1])) << 32) | __float_as_uint(acc[2 * j]);
+    const uint64_t v2 = (static_cast<uint64_t>(v[2 * j + 1]) << 32) | v[2 * j];
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a2) : "l"(v2), "l"(s2));
+    acc[2 * j] = __uint_as_float(static_cast<uint32_t>(a2));
+    acc[2 * j + 1] = __uint_as_float(static_cast<uint32_t>(a2 >> 32));
+  }
+}
+
+template <int kKind, int kCG>
 __global__ void __launch_bounds__(THREADS, 1)
     bb_lowp_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
                         const Params p) {
-  using C = Cfg<kKind>;
-  if (blockDim.x != THREADS) {
+  using C = Cfg<kKind, kCG>;
+  constexpr int STAGES = C::STAGES;
+  constexpr bool kPair = kCG == 2;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  if (blockDim.x != THREADS || (kPair && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
     if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kDevBadLaunch);
     return;
   }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem_a + STAGES * A_BYTES;
-  uint8_t* smem_sfa = smem_b + STAGES * B_BYTES;          // NVFP4 only
-  uint8_t* smem_sfb = smem_sfa + STAGES * SFA_BYTES;      // NVFP4 only
+  uint8_t* smem_b = smem_a + STAGES * C::A_BYTES;
+  uint8_t* smem_sfa = smem_b + STAGES * C::B_BYTES;        // NVFP4 only
+  uint8_t* smem_sfb = smem_sfa + STAGES * C::SFA_BYTES;    // NVFP4 only
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;       // [2]
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2], in the leader CTA
   uint64_t* mma_done = bars + 2 * STAGES + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const bool leader = rank == 0;
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_b);
+    if constexpr (kKind == kNvfp4) {
+      prefetch_tmap(&tm_sfa);
+      prefetch_tmap(&tm_sfb);
+    }
   }
   if (warp == 1 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -215,78 +297,97 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), EPI_WARPS);
+      mbar_init(smem_u32(&acc_empty[b]), EPI_WARPS * kCG);
     }
     mbar_init(smem_u32(mma_done), 1);
     fence_mbarrier_init_cluster();
   }
   if (warp == 1) {
-    tmem_alloc<1>(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish<1>();
+    tmem_alloc<kCG>(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish<kCG>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const int cluster_idx = blockIdx.x / kCG;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      bool ok = true;
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-        int m_blk, n_blk;
-        tile_coords(p, t, m_blk, n_blk);
-        const int rb_b = 2 * n_blk;  // first 128-row block of B's scales
-        const int sfb_blocks = kKind == kNvfp4 ? min(2, p.rb_n - rb_b) : 0;
-        for (int ks = 0; ks < p.k_stages; ++ks) {
-          if (!bb_wait(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&full[stage]);
-          uint32_t bytes = A_BYTES + B_BYTES;
-          if constexpr (kKind == kNvfp4) bytes += SFA_BYTES + sfb_blocks * (SFB_BYTES / 2);
-          mbar_arrive_expect_tx(fb, bytes);
-          tma_load_2d(smem_u32(smem_a + stage * A_BYTES), &tm_a, fb, ks * ROW_BYTES, m_blk * BM);
-          tma_load_2d(smem_u32(smem_b + stage * B_BYTES), &tm_b, fb, ks * ROW_BYTES, n_blk * BN);
+    // The whole warp runs the loop and waits; one elected lane issues.
+    bool ok = true;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = cluster_idx; ok && t < p.num_tiles; t += p.num_clusters) {
+      int m_blk, n_blk;
+      tile_coords(p, t, m_blk, n_blk);
+      const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * BM;
+      const int b_row = n_blk * C::TILE_N + static_cast<int>(rank) * C::B_ROWS;
+      const int sfa_blk = m_blk * kCG + static_cast<int>(rank);
+      for (int ks = 0; ks < p.k_stages; ++ks) {
+        if (!bb_wait_warp<kPair>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          const uint32_t fb_own = smem_u32(&full[stage]);
+          const uint32_t fb = kPair ? mapa_shared(fb_own, 0) : fb_own;
+          if (leader) mbar_arrive_expect_tx(fb_own, C::STAGE_BYTES * kCG);
+          load_2d<kCG>(smem_u32(smem_a + stage * C::A_BYTES), &tm_a, fb, ks * ROW_BYTES, a_row);
+          load_2d<kCG>(smem_u32(smem_b + stage * C::B_BYTES), &tm_b, fb, ks * ROW_BYTES, b_row);
           if constexpr (kKind == kNvfp4) {
-            const int64_t kg0 = static_cast<int64_t>(ks) * 4;
-            bulk_load(smem_u32(smem_sfa + stage * SFA_BYTES),
-                      p.sfa + (static_cast<int64_t>(m_blk) * p.k_groups + kg0) * 512, SFA_BYTES, fb);
-            for (int r = 0; r < sfb_blocks; ++r)
-              bulk_load(smem_u32(smem_sfb + stage * SFB_BYTES + r * (SFB_BYTES / 2)),
-                        p.sfb + (static_cast<int64_t>(rb_b + r) * p.k_groups + kg0) * 512, SFB_BYTES / 2, fb);
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+            // Scale atoms as rows of 8-byte words: one row per 128-row block,
+            // K/64 atoms of 64 words each; a stage is 4 atoms (256 words).
+            load_2d<kCG>(smem_u32(smem_sfa + stage * C::SFA_BYTES), &tm_sfa, fb, ks * 256, sfa_blk);
+            load_2d<kCG>(smem_u32(smem_sfb + stage * C::SFB_BYTES), &tm_sfb, fb, ks * 256, 2 * n_blk);
           }
         }
-      }
-      if (ok) {
-        for (int i = 0; i < STAGES; ++i) {
-          if (!bb_wait(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
-      } else {
-        bounded_sleep_ns(2000000);
       }
     }
+    if (ok) {
+      // Tail: wait until the MMA has released every stage, so no commit
+      // arrival can still be in flight towards this CTA when it exits.
+      for (int i = 0; i < STAGES; ++i) {
+        if (!bb_wait_warp<kPair>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    } else if (lane == 0) {
+      bounded_sleep_ns(2000000);  // aborted: let copies already issued land
+    }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    // Whole warp runs the loop and waits; one elected lane issues the scale
+    // copies, MMAs and commits of each stage (always the same lane: elect.sync
+    // picks the lowest active lane of the converged warp).
+    if (leader) {
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_iter = 0;  // NVFP4: tiles; FP8: K blocks (partial buffers)
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+      // Stage-0 descriptors; stage s adds s times the stage size (in 16-byte
+      // units, the unit of the descriptors' start-address field).
+      const uint64_t a_desc0 = sw128_kmajor_desc(smem_u32(smem_a));
+      const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(smem_b));
+      const uint64_t sfa_desc0 = sf_atom_desc(smem_u32(smem_sfa));
+      const uint64_t sfb_desc0 = sf_atom_desc(smem_u32(smem_sfb));
+      const uint32_t sf_cols0 = tmem_base + kSfBase;
+      auto commit_both = [&](uint64_t* bar) {
+        const uint32_t a = smem_u32(bar);
+        umma_commit<kCG>(a);
+        if constexpr (kPair) umma_commit<kCG>(mapa_shared(a, 1));
+      };
+      for (int t = cluster_idx; ok && t < p.num_tiles; t += p.num_clusters) {
         if constexpr (kKind == kNvfp4) {
-          if (!bb_wait(smem_u32(&acc_empty[0]), (acc_iter & 1u) ^ 1u, p.status, kDevTimeoutMma)) {
+          if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[0]), (acc_iter & 1u) ^ 1u, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -297,48 +398,48 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t buf = 0;
           if constexpr (kKind == kFp8Block) {
             buf = acc_iter & 1u;
-            if (!bb_wait(smem_u32(&acc_empty[buf]), ((acc_iter >> 1) & 1u) ^ 1u, p.status, kDevTimeoutMma)) {
+            if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[buf]), ((acc_iter >> 1) & 1u) ^ 1u, p.status,
+                                     kDevTimeoutMma)) {
               ok = false;
               break;
             }
+            tc_fence_after();
             d_tmem = tmem_base + buf * 256u;
           }
-          if (!bb_wait(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
+          if (!bb_wait_warp<kPair>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * B_BYTES);
-          if constexpr (kKind == kNvfp4) {
-            const uint32_t sf_cols = tmem_base + kSfBase + stage * kSfStageCols;
-            const uint32_t sfa_s = smem_u32(smem_sfa + stage * SFA_BYTES);
-            const uint32_t sfb_s = smem_u32(smem_sfb + stage * SFB_BYTES);
+          if (elect_one()) {
+            const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * (C::A_BYTES >> 4);
+            const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * (C::B_BYTES >> 4);
+            if constexpr (kKind == kNvfp4) {
+              const uint32_t sf_cols = sf_cols0 + stage * kSfStageCols;
+              const uint64_t sfa_desc = sfa_desc0 + static_cast<uint64_t>(stage) * (C::SFA_BYTES >> 4);
+              const uint64_t sfb_desc = sfb_desc0 + static_cast<uint64_t>(stage) * (C::SFB_BYTES >> 4);
+              constexpr uint32_t idesc = idesc_nvf4(C::TILE_M, C::TILE_N);
+              // Per K step: its three scale copies, then its MMA (copies and
+              // MMAs of one thread execute in issue order).
 #pragma unroll
-            for (int g = 0; g < C::MMAS; ++g) {
-              tmem_cp_atom(sf_cols + 4 * g, sfa_s + g * 512);
-              tmem_cp_atom(sf_cols + 16 + 8 * g, sfb_s + g * 512);
-              tmem_cp_atom(sf_cols + 16 + 8 * g + 4, sfb_s + SFB_BYTES / 2 + g * 512);
-            }
-            constexpr uint32_t idesc = idesc_nvf4(BM, BN);
+              for (int g = 0; g < C::MMAS; ++g) {
+                tmem_cp_desc<kCG>(sf_cols + 4 * g, sfa_desc + g * (SF_ATOM >> 4));
+                tmem_cp_desc<kCG>(sf_cols + 16 + 8 * g, sfb_desc + g * (SF_ATOM >> 4));
+                tmem_cp_desc<kCG>(sf_cols + 20 + 8 * g, sfb_desc + (C::SFB_BYTES / 2 + g * SF_ATOM) / 16);
+                mma_nvf4<kCG>(d_tmem, a_desc + 2 * g, b_desc + 2 * g, idesc, sf_cols + 4 * g, sf_cols + 16 + 8 * g,
+                              (ks | g) != 0 ? 1u : 0u);
+              }
+            } else {
+              constexpr uint32_t idesc = idesc_f8(C::TILE_M, C::TILE_N);
 #pragma unroll
-            for (int g = 0; g < C::MMAS; ++g) {
-              mma_nvf4(d_tmem, sw128_kmajor_desc(a_addr + g * 32), sw128_kmajor_desc(b_addr + g * 32), idesc,
-                       sf_cols + 4 * g, sf_cols + 16 + 8 * g, (ks != 0 || g != 0) ? 1u : 0u);
+              for (int g = 0; g < C::MMAS; ++g)
+                mma_f8<kCG>(d_tmem, a_desc + 2 * g, b_desc + 2 * g, idesc, g != 0 ? 1u : 0u);
             }
-          } else {
-            constexpr uint32_t idesc = idesc_f8(BM, BN);
-#pragma unroll
-            for (int g = 0; g < C::MMAS; ++g) {
-              mma_f8(d_tmem, sw128_kmajor_desc(a_addr + g * 32), sw128_kmajor_desc(b_addr + g * 32), idesc,
-                     g != 0 ? 1u : 0u);
-            }
+            commit_both(&empty[stage]);
+            if constexpr (kKind == kFp8Block) commit_both(&acc_full[buf]);
           }
-          umma_commit<1>(smem_u32(&empty[stage]));
-          if constexpr (kKind == kFp8Block) {
-            umma_commit<1>(smem_u32(&acc_full[buf]));
-            ++acc_iter;
-          }
+          __syncwarp();
+          if constexpr (kKind == kFp8Block) ++acc_iter;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -346,12 +447,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         if constexpr (kKind == kNvfp4) {
-          umma_commit<1>(smem_u32(&acc_full[0]));
+          if (elect_one()) commit_both(&acc_full[0]);
+          __syncwarp();
           ++acc_iter;
         }
       }
-      umma_commit<1>(smem_u32(mma_done));
-      bb_wait(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
+      // Drain: every MMA issued so far must finish before TMEM is freed.
+      if (elect_one()) umma_commit<kCG>(smem_u32(mma_done));
+      __syncwarp();
+      bb_wait_warp(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -363,16 +467,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     auto release = [&](uint32_t buf) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+      if (lane == 0) {
+        const uint32_t eb = smem_u32(&acc_empty[buf]);
+        if constexpr (kPair) {
+          mbar_arrive_cluster(mapa_shared(eb, 0));
+        } else {
+          mbar_arrive(eb);
+        }
+      }
     };
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+    for (int t = cluster_idx; ok && t < p.num_tiles; t += p.num_clusters) {
       int m_blk, n_blk;
       tile_coords(p, t, m_blk, n_blk);
-      const int row = m_blk * BM + q * 32 + lane;
-      const int col0 = n_blk * BN + half * 128;
+      const int row = m_blk * C::TILE_M + static_cast<int>(rank) * BM + q * 32 + lane;
+      const int col0 = n_blk * C::TILE_N + half * 128;
       uint32_t pk[64];
       if constexpr (kKind == kNvfp4) {
-        if (!bb_wait(smem_u32(&acc_full[0]), acc_iter & 1u, p.status, kDevTimeoutEpilogue)) break;
+        if (!bb_wait_warp<kPair>(smem_u32(&acc_full[0]), acc_iter & 1u, p.status, kDevTimeoutEpilogue)) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_off + half * 128;
 #pragma unroll
@@ -389,9 +500,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         const float* sa = reinterpret_cast<const float*>(p.sfa);
         const float* sb = reinterpret_cast<const float*>(p.sfb);
-        const int rb_n = (p.n + 127) / 128;
-        const int nb = min(2 * n_blk + half, rb_n - 1);  // ragged N: columns past N are never stored
-        const float* sa_row = sa + static_cast<int64_t>(m_blk) * p.k_stages;
+        // Ragged edges: rows / columns past M / N are never stored, any valid
+        // scale row serves them.
+        const int mb = min(m_blk * kCG + static_cast<int>(rank), p.rb_m - 1);
+        const int nb = min(2 * n_blk + half, p.rb_n - 1);
+        const float* sa_row = sa + static_cast<int64_t>(mb) * p.k_stages;
         const float* sb_row = sb + static_cast<int64_t>(nb) * p.k_stages;
         float acc[128];
 #pragma unroll
@@ -401,7 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float s = s_next;
           if (ks + 1 < p.k_stages) s_next = __ldg(sa_row + ks + 1) * __ldg(sb_row + ks + 1);
           const uint32_t buf = acc_iter & 1u;
-          if (!bb_wait(smem_u32(&acc_full[buf]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) {
+          if (!bb_wait_warp<kPair>(smem_u32(&acc_full[buf]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) {
             ok = false;
             break;
           }
@@ -413,8 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_ld_32x32b_x32(taddr + 32 * c, r0);
             tmem_ld_wait();
             if (c == 3) release(buf);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[32 * c + j] = fmaf(__uint_as_float(r0[j]), s, acc[32 * c + j]);
+            promote32(acc + 32 * c, r0, s);
           }
           ++acc_iter;
         }
@@ -428,9 +540,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
-    tmem_dealloc<1>(tmem_base, TMEM_COLS);
+    tmem_dealloc<kCG>(tmem_base, TMEM_COLS);
   }
 }
 
@@ -439,14 +553,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 struct bb_lowp_plan {
   int kind = 0;
+  int cg = 1;
+  int stages = 0;
   int64_t m = 0, n = 0, k = 0;
-  const void* a = nullptr;
-  const void* b = nullptr;
-  const void* sfa = nullptr;
-  const void* sfb = nullptr;
-  void* d = nullptr;
   cudaStream_t stream = nullptr;
-  CUtensorMap tm_a{}, tm_b{};
+  CUtensorMap tm_a{}, tm_b{}, tm_sfa{}, tm_sfb{};
   bb::lowp::Params params{};
   int grid = 0;
   int smem_bytes = 0;
@@ -459,25 +570,81 @@ using namespace bb::lowp;
 
 namespace {
 
-template <int kKind>
-int launch_kind(const bb_lowp_plan& pl) {
-  auto kern = bb_lowp_gemm_kernel<kKind>;
-  static bool attr_set = false;  // one attribute call per kernel and process
-  if (!attr_set) {
-    BB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<kKind>::SMEM_BYTES));
-    attr_set = true;
-  }
+template <int kKind, int kCG>
+cudaLaunchConfig_t launch_config(const bb_lowp_plan& pl, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = Cfg<kKind>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = Cfg<kKind, kCG>::SMEM_BYTES;
   cfg.stream = pl.stream;
-  cfg.numAttrs = 0;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kern, pl.tm_a, pl.tm_b, pl.params), "launch bb_lowp_gemm_kernel");
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+template <int kKind, int kCG>
+int set_attributes() {
+  static bool done = false;  // one attribute call per kernel and process
+  if (!done) {
+    BB_CUDA_TRY(cudaFuncSetAttribute(bb_lowp_gemm_kernel<kKind, kCG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg<kKind, kCG>::SMEM_BYTES));
+    done = true;
+  }
+  return BB_OK;
+}
+
+template <int kKind, int kCG>
+int launch_kind(const bb_lowp_plan& pl) {
+  int rc = set_attributes<kKind, kCG>();
+  if (rc != BB_OK) return rc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_config<kKind, kCG>(pl, attr);
+  return check_cuda(cudaLaunchKernelEx(&cfg, bb_lowp_gemm_kernel<kKind, kCG>, pl.tm_a, pl.tm_b, pl.tm_sfa, pl.tm_sfb,
+                                       pl.params),
+                    "launch bb_lowp_gemm_kernel");
 }
 
 int launch(const bb_lowp_plan& pl) {
-  return pl.kind == kNvfp4 ? launch_kind<kNvfp4>(pl) : launch_kind<kFp8Block>(pl);
+  if (pl.kind == kNvfp4) return pl.cg == 2 ? launch_kind<kNvfp4, 2>(pl) : launch_kind<kNvfp4, 1>(pl);
+  return pl.cg == 2 ? launch_kind<kFp8Block, 2>(pl) : launch_kind<kFp8Block, 1>(pl);
+}
+
+// Clusters of kCG CTAs resident at once (one CTA per SM: the shared-memory
+// ring takes the whole SM).
+template <int kKind, int kCG>
+int max_clusters(const bb_lowp_plan& pl, int sm_count) {
+  int clusters = sm_count / kCG;
+  if (kCG > 1 && set_attributes<kKind, kCG>() == BB_OK) {
+    bb_lowp_plan probe = pl;
+    probe.grid = kCG * clusters;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = launch_config<kKind, kCG>(probe, attr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, bb_lowp_gemm_kernel<kKind, kCG>, &cfg) == cudaSuccess && n > 0) {
+      clusters = n;
+    } else {
+      cudaGetLastError();
+    }
+  }
+  return clusters;
+}
+
+template <int kKind, int kCG>
+void plan_geometry(bb_lowp_plan& h, int sm_count) {
+  using C = Cfg<kKind, kCG>;
+  h.stages = C::STAGES;
+  h.smem_bytes = C::SMEM_BYTES;
+  Params& p = h.params;
+  p.tiles_m = static_cast<int32_t>((h.m + C::TILE_M - 1) / C::TILE_M);
+  p.tiles_n = static_cast<int32_t>((h.n + C::TILE_N - 1) / C::TILE_N);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  const int clusters = max_clusters<kKind, kCG>(h, sm_count);
+  p.num_clusters = p.num_tiles < clusters ? p.num_tiles : clusters;
+  h.grid = p.num_clusters * kCG;
 }
 
 }  // namespace
@@ -512,7 +679,7 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
       set_error("bb_lowp_plan_create: null operand pointer");
       return BB_ERR_ARGUMENT;
     }
-    if (m <= 0 || n <= 0 || k <= 0 || m > (int64_t(1) << 31) || n > (int64_t(1) << 31) || k > (int64_t(1) << 31)) {
+    if (m <= 0 || n <= 0 || k <= 0 || m > (int64_t(1) << 30) || n > (int64_t(1) << 30) || k > (int64_t(1) << 30)) {
       set_error("bb_lowp_plan_create: extents out of range (m=%lld n=%lld k=%lld)", (long long)m, (long long)n,
                 (long long)k);
       return BB_ERR_ARGUMENT;
@@ -548,14 +715,22 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     h->m = m;
     h->n = n;
     h->k = k;
-    h->a = a;
-    h->b = b;
-    h->sfa = sfa;
-    h->sfb = sfb;
-    h->d = d;
     h->stream = static_cast<cudaStream_t>(stream);
+    // CTA pairs (256-row tiles) unless A has a single 128-row block;
+    // BB_LOWP_CTA_GROUP=1|2 forces one.
+    h->cg = m > 128 ? 2 : 1;
+    if (const char* env = std::getenv("BB_LOWP_CTA_GROUP")) {
+      if (env[0] == '1') h->cg = 1;
+      if (env[0] == '2') h->cg = 2;
+    }
+    if (kind == kNvfp4) {
+      if (h->cg == 2) plan_geometry<kNvfp4, 2>(*h, dev.sm_count); else plan_geometry<kNvfp4, 1>(*h, dev.sm_count);
+    } else {
+      if (h->cg == 2) plan_geometry<kFp8Block, 2>(*h, dev.sm_count); else plan_geometry<kFp8Block, 1>(*h, dev.sm_count);
+    }
     // Operands are byte arrays: K / 2 bytes per row for E2M1, K for E4M3.
     const uint64_t row_bytes = kind == BB_LOWP_NVFP4 ? k / 2 : k;
+    const uint64_t rb_m = (m + 127) / 128, rb_n = (n + 127) / 128;
     {
       const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(m)};
       const uint64_t strides[1] = {row_bytes};
@@ -566,9 +741,27 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     if (rc == BB_OK) {
       const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(n)};
       const uint64_t strides[1] = {row_bytes};
-      const uint32_t box[2] = {ROW_BYTES, BN};
+      const uint32_t box[2] = {ROW_BYTES, static_cast<uint32_t>(256 / h->cg)};
       rc = encode_tiled(&h->tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 2, b, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    }
+    if (rc == BB_OK && kind == BB_LOWP_NVFP4) {
+      // Scale atoms viewed as rows of 8-byte words, one row per 128-row block
+      // (K words: K/64 atoms of 64 words); a stage's box is 256 words (4 atoms).
+      const uint64_t strides[1] = {static_cast<uint64_t>(k) * 8};
+      const uint64_t dims_a[2] = {static_cast<uint64_t>(k), rb_m};
+      const uint32_t box_a[2] = {256, 1};
+      rc = encode_tiled(&h->tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, 2, sfa, dims_a, strides, box_a,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+      if (rc == BB_OK) {
+        const uint64_t dims_b[2] = {static_cast<uint64_t>(k), rb_n};
+        const uint32_t box_b[2] = {256, 2};
+        rc = encode_tiled(&h->tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, 2, sfb, dims_b, strides, box_b,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+      }
+    } else {
+      h->tm_sfa = h->tm_a;  // unused by the FP8 kernel
+      h->tm_sfb = h->tm_b;
     }
     if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
     if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
@@ -581,31 +774,27 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     p.m = static_cast<int32_t>(m);
     p.n = static_cast<int32_t>(n);
     p.k = static_cast<int32_t>(k);
-    p.tiles_m = static_cast<int32_t>((m + BM - 1) / BM);
-    p.tiles_n = static_cast<int32_t>((n + BN - 1) / BN);
-    p.num_tiles = p.tiles_m * p.tiles_n;
     p.k_stages = static_cast<int32_t>(k / k_step);
-    p.k_groups = static_cast<int32_t>(k / 64);
-    p.rb_n = static_cast<int32_t>((n + 127) / 128);
+    p.rb_m = static_cast<int32_t>(rb_m);
+    p.rb_n = static_cast<int32_t>(rb_n);
     p.sfa = static_cast<const uint8_t*>(sfa);
     p.sfb = static_cast<const uint8_t*>(sfb);
     p.global_scale = global_scale;
     p.d = static_cast<__nv_bfloat16*>(d);
     p.status = h->status_dev;
-    h->grid = p.num_tiles < dev.sm_count ? p.num_tiles : dev.sm_count;
-    h->smem_bytes = kind == BB_LOWP_NVFP4 ? Cfg<kNvfp4>::SMEM_BYTES : Cfg<kFp8Block>::SMEM_BYTES;
     if (info) {
       info->kind = kind;
-      info->tile_m = BM;
-      info->tile_n = BN;
+      info->tile_m = 128 * h->cg;
+      info->tile_n = 256;
       info->tile_k = k_step;
-      info->stages = STAGES;
+      info->stages = h->stages;
       info->grid_ctas = h->grid;
       info->num_tiles = p.num_tiles;
       info->smem_bytes = h->smem_bytes;
       info->tmem_columns = TMEM_COLS;
       info->threads_per_cta = THREADS;
-      for (int i = 0; i < 6; ++i) info->reserved[i] = 0;
+      info->cta_group = h->cg;
+      for (int i = 0; i < 5; ++i) info->reserved[i] = 0;
     }
     *plan = h;
     return BB_OK;

@@ -135,6 +135,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, with a suspend-time hint: a thread whose phase is not complete yet
+// may sleep in the instruction (up to `hint_ns`) instead of spinning, and
+// wakes when the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster_hint(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Cluster-scope acquire variant, for barriers that peer CTAs arrive on.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
   uint32_t ok;
@@ -171,6 +196,36 @@ __device__ __forceinline__ bool bb_wait(uint32_t addr, uint32_t parity, int* sta
       if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) return false;
     }
   }
+}
+
+// Warp-wide bounded wait: every lane of the (converged) warp polls with a
+// 1 ms suspend hint; lane 0's outcome is returned to all lanes, so loops
+// around it stay warp-uniform. Issue loops built this way (whole warp waits,
+// one elect.sync lane issues) keep tcgen05 issue well ahead of execution; a
+// lone lane looping inside a divergent branch issues markedly slower.
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool bb_wait_warp(uint32_t addr, uint32_t parity, int* status, int code,
+                                             bool honor_abort = true, uint64_t budget_ns = kWaitBudgetNs) {
+  constexpr uint32_t kHint = 1000000u;
+  auto probe = [&]() {
+    return kClusterScope ? mbar_try_wait_cluster_hint(addr, parity, kHint) : mbar_try_wait_hint(addr, parity, kHint);
+  };
+  bool ok = probe();
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      if (probe()) {
+        ok = true;
+        break;
+      }
+      if (globaltimer_ns() - t0 > budget_ns) {
+        if (status && (threadIdx.x % 32) == 0) atomicCAS(status, 0, code);
+        break;
+      }
+      if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) break;
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
 // Sleep for about `ns` nanoseconds (bounded drain for copies in flight).

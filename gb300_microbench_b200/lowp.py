@@ -237,3 +237,53 @@ class LowpGemmPlan:
             self.close()
         except Exception:
             pass
+
+
+class CublasLtLowpPlan:
+    """cuBLASLt's block-scaled GEMM on the same operands (the comparator, a
+    library call; bb_cmp_lowp_plan_create of include/b200cmp.h).
+
+    ``fp8_scales_kmajor`` chooses how the FP32 128 x 128 block scales are
+    handed over: True passes them as stored ([row block][K block]), False
+    passes the transpose ([K block][row block])."""
+
+    def __init__(self, kind: str, a, b, d: torch.Tensor, autotune: bool = False,
+                 stream: torch.cuda.Stream | None = None, fp8_scales_kmajor: bool = False):
+        if kind not in KINDS:
+            raise ValueError(f"unknown kind {kind!r}")
+        self._lib = nat.cmp_lib()
+        self.stream = stream if stream is not None else torch.cuda.current_stream(d.device)
+        m, n, k = a.rows, b.rows, a.k
+        if kind == "nvfp4":
+            sfa, sfb, gscale = a.atoms, b.atoms, a.tensor_scale * b.tensor_scale
+        else:
+            sfa, sfb, gscale = a.scales, b.scales, 1.0
+            if not fp8_scales_kmajor:
+                sfa, sfb = sfa.t().contiguous(), sfb.t().contiguous()
+        self._keep = (a, b, sfa, sfb, d)
+        handle = ctypes.c_void_p()
+        info = nat.CmpInfo()
+        rc = self._lib.bb_cmp_lowp_plan_create(KINDS[kind], m, n, k, a.data.data_ptr(), b.data.data_ptr(),
+                                               sfa.data_ptr(), sfb.data_ptr(), float(gscale), d.data_ptr(),
+                                               1 if autotune else 0, self.stream.cuda_stream, ctypes.byref(handle),
+                                               ctypes.byref(info))
+        if rc != 0:
+            raise nat.NativeCallError("bb_cmp_lowp_plan_create", rc, self._lib.bb_cmp_last_error().decode())
+        self._handle = handle
+        self.info = info.as_dict()
+
+    def run(self, iterations: int = 1) -> None:
+        rc = self._lib.bb_cmp_execute_n(self._handle, int(iterations))
+        if rc != 0:
+            raise nat.NativeCallError("bb_cmp_execute_n", rc, self._lib.bb_cmp_last_error().decode())
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            self._lib.bb_cmp_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -4,10 +4,13 @@ kernel, a few launches, nothing else.
     python -m gb300_microbench_b200.profile_cases gemm M N K VARIANT [out_dtype]
     python -m gb300_microbench_b200.profile_cases copy METHOD STAGES BIF_KIB ROW_BYTES MIB
     python -m gb300_microbench_b200.profile_cases umma CTA_GROUP N DEPTH ITERATIONS
+    python -m gb300_microbench_b200.profile_cases lowp KIND M N K [CTA_GROUP]
 
 gemm: N(0,1) BF16 operands (torch.Generator seed 0), 4 launches of the plan.
 copy: a MIB-MiB seeded uniform-u32 buffer, 3 one-pass launches.
 umma: the reference's integer operands, 2 launches.
+lowp: KIND nvfp4 or fp8_block128, quantised N(0,1) operands (seed 0),
+      4 launches of the block-scaled plan (CTA_GROUP 1 or 2 forces the tile).
 Each prints "ok" and exits 0 when the kernel reported no device error.
 """
 from __future__ import annotations
@@ -56,6 +59,22 @@ def main(argv: list[str] | None = None) -> int:
         for _ in range(2):
             probe.launch(iters)
         probe.result()
+    elif what == "lowp":
+        import os
+
+        from . import lowp
+
+        kind, (m, n, k) = args[0], (int(x) for x in args[1:4])
+        if len(args) > 4:
+            os.environ["BB_LOWP_CTA_GROUP"] = args[4]
+        x, y = lowp.config4_inputs(m, n, k, seed=0, device="cuda")
+        op = lowp.Nvfp4Operand if kind == "nvfp4" else lowp.Fp8BlockOperand
+        a, b = op(x), op(y)
+        del x, y
+        d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        plan = lowp.LowpGemmPlan(kind, a, b, d)
+        plan.run(4)
+        plan.synchronize()
     else:
         print(__doc__)
         return 2

@@ -250,14 +250,15 @@ enum { BB_LOWP_NVFP4 = 1, BB_LOWP_FP8_BLOCK128 = 2 };
 
 typedef struct bb_lowp_info {
   int64_t kind;
-  int64_t tile_m, tile_n, tile_k; /* output tile and K elements per stage */
+  int64_t tile_m, tile_n, tile_k; /* output tile (of a CTA or CTA pair), K elements per stage */
   int64_t stages;
   int64_t grid_ctas;
   int64_t num_tiles;
   int64_t smem_bytes;
   int64_t tmem_columns;
   int64_t threads_per_cta;
-  int64_t reserved[6];
+  int64_t cta_group; /* 1: one CTA per tile, 2: CTA pair (cta_group::2) */
+  int64_t reserved[5];
 } bb_lowp_info;
 
 typedef struct bb_lowp_plan bb_lowp_plan;

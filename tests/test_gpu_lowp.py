@@ -64,12 +64,17 @@ def _run(kind, a, b, dev):
     return d.cpu()
 
 
-EXACT_SHAPES = [(128, 256, 256), (256, 512, 512), (384, 256, 1024), (200, 264, 512), (1024, 768, 768)]
+EXACT_SHAPES = [(128, 256, 256), (256, 512, 512), (384, 256, 1024), (200, 264, 512), (1024, 768, 768),
+                (520, 136, 256)]
 
 
+@pytest.mark.parametrize("cta_group", ["1", "2"])
 @pytest.mark.parametrize("kind", ["nvfp4", "fp8_block128"])
 @pytest.mark.parametrize("mnk", EXACT_SHAPES)
-def test_exact(cuda_device, kind, mnk):
+def test_exact(cuda_device, kind, mnk, cta_group, monkeypatch):
+    """Both tile shapes (BB_LOWP_CTA_GROUP forces 128 x 256 single-CTA or
+    256 x 256 CTA-pair tiles)."""
+    monkeypatch.setenv("BB_LOWP_CTA_GROUP", cta_group)
     m, n, k = mnk
     if kind == "nvfp4" and k % 256:
         pytest.skip("NVFP4 needs K % 256 == 0")
