@@ -716,9 +716,13 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     h->n = n;
     h->k = k;
     h->stream = static_cast<cudaStream_t>(stream);
-    // CTA pairs (256-row tiles) unless A has a single 128-row block;
+    // NVFP4: CTA pairs (256-row tiles) unless A has a single 128-row block.
+    // FP8: single CTAs. Its epilogue promotes every 128-wide K block; the
+    // MMA -> epilogue -> MMA hand-off of the two TMEM partial buffers already
+    // limits one CTA, and across a pair (peer arrivals through the cluster)
+    // it costs far more than the halved B traffic saves.
     // BB_LOWP_CTA_GROUP=1|2 forces one.
-    h->cg = m > 128 ? 2 : 1;
+    h->cg = (kind == BB_LOWP_NVFP4 && m > 128) ? 2 : 1;
     if (const char* env = std::getenv("BB_LOWP_CTA_GROUP")) {
       if (env[0] == '1') h->cg = 1;
       if (env[0] == '2') h->cg = 2;

@@ -238,22 +238,24 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      bool ok = true;
-      int stage = 0;
-      uint32_t phase = 0;
-      const uint32_t full_target_rank = 0;
-      WorkItem it;
-      for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx) {
-        int l, m_blk, n_blk;
-        tile_coords(p, it.tile, l, m_blk, n_blk);
-        const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM;
-        const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_BOX_ROWS;
-        for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
-            ok = false;
-            break;
-          }
+    // The whole warp runs the loop and waits; one elected lane issues (a lone
+    // lane looping inside a divergent branch issues markedly slower).
+    bool ok = true;
+    int stage = 0;
+    uint32_t phase = 0;
+    const uint32_t full_target_rank = 0;
+    WorkItem it;
+    for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx) {
+      int l, m_blk, n_blk;
+      tile_coords(p, it.tile, l, m_blk, n_blk);
+      const int a_row = m_blk * C::TILE_M + static_cast<int>(rank) * C::BM;
+      const int b_row = n_blk * kBN + static_cast<int>(rank) * C::B_BOX_ROWS;
+      for (int kb = it.kb0; kb < it.kb1; ++kb) {
+        if (!bb_wait_warp<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
           const uint32_t fb = smem_u32(&full[stage]);
           if (mma_cta) mbar_arrive_expect_tx(fb, C::STAGE_BYTES * kCG);
           const uint32_t da = smem_u32(smem_a + stage * C::A_BYTES);
@@ -270,31 +272,36 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
             for (int h = 0; h < C::N_SUB; ++h)
               tma_load_3d(db + h * C::B_SUB_BYTES, &tm_b, fb, kb * kBK, b_row + h * C::MMA_N, l);
           }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      if (ok) {
-        // Tail: wait until the MMA has released every stage, so no commit
-        // arrival can still be in flight towards this CTA when it exits.
-        for (int i = 0; i < STAGES; ++i) {
-          if (!bb_wait<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+    }
+    if (ok) {
+      // Tail: wait until the MMA has released every stage, so no commit
+      // arrival can still be in flight towards this CTA when it exits.
+      for (int i = 0; i < STAGES; ++i) {
+        if (!bb_wait_warp<kCG == 2>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
-      } else {
-        // Aborted: let any TMA copy already issued land before teardown.
-        bounded_sleep_ns(2000000);
       }
+    } else if (lane == 0) {
+      // Aborted: let any TMA copy already issued land before teardown.
+      bounded_sleep_ns(2000000);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (mma_cta && lane == 0) {
+    // Whole warp loops and waits; the elected lane (always the lowest lane of
+    // the converged warp, so its commits track all of its MMAs) issues.
+    if (mma_cta) {
       constexpr uint32_t idesc = make_idesc_bf16_f32(C::TILE_M, C::MMA_N);
+      const uint64_t a_desc0 = sw128_kmajor_desc(smem_u32(smem_a));
+      const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(smem_b));
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
@@ -303,45 +310,53 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
       for (int idx = 0; ok && next_item(p, cluster_idx, idx, it); ++idx, ++acc_iter) {
         const uint32_t acc = acc_iter % C::ACC_BUFS;
         const uint32_t acc_phase = (acc_iter / C::ACC_BUFS) & 1u;
-        if (!bb_wait<kCG == 2>(smem_u32(&tmem_empty[acc]), acc_phase ^ 1u, p.status, kDevTimeoutMma)) {
+        if (!bb_wait_warp<kCG == 2>(smem_u32(&tmem_empty[acc]), acc_phase ^ 1u, p.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          if (!bb_wait<kCG == 2>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
+          if (!bb_wait_warp<kCG == 2>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * C::B_BYTES);
+          if (elect_one()) {
+            // Descriptors advance by adds in 16-byte units (the start-address
+            // field's unit): 32 bytes (2 units) per K16 step.
+            const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * (C::A_BYTES >> 4);
+            const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * (C::B_BYTES >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
+            for (int kk = 0; kk < kBK / 16; ++kk) {
 #pragma unroll
-            for (int h = 0; h < C::N_SUB; ++h) {
-              umma_f16<kCG>(d_tmem + h * C::MMA_N, sw128_kmajor_desc(a_addr + kk * 32),
-                            sw128_kmajor_desc(b_addr + h * C::B_SUB_BYTES + kk * 32), idesc,
-                            (kb != it.kb0 || kk != 0) ? 1u : 0u);
+              for (int h = 0; h < C::N_SUB; ++h) {
+                umma_f16<kCG>(d_tmem + h * C::MMA_N, a_desc + 2 * kk, b_desc + h * (C::B_SUB_BYTES >> 4) + 2 * kk,
+                              idesc, (kb != it.kb0 || kk != 0) ? 1u : 0u);
+              }
             }
+            const uint32_t eb = smem_u32(&empty[stage]);
+            umma_commit<kCG>(eb);
+            if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(eb, 1));
           }
-          const uint32_t eb = smem_u32(&empty[stage]);
-          umma_commit<kCG>(eb);
-          if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(eb, 1));
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        const uint32_t fb = smem_u32(&tmem_full[acc]);
-        umma_commit<kCG>(fb);
-        if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(fb, 1));
+        if (elect_one()) {
+          const uint32_t fb = smem_u32(&tmem_full[acc]);
+          umma_commit<kCG>(fb);
+          if constexpr (kCG == 2) umma_commit<kCG>(mapa_shared(fb, 1));
+        }
+        __syncwarp();
       }
       // Drain: every MMA issued so far must finish before TMEM is freed.
-      umma_commit<kCG>(smem_u32(mma_done));
-      bb_wait(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
+      if (elect_one()) umma_commit<kCG>(smem_u32(mma_done));
+      __syncwarp();
+      bb_wait_warp(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -614,7 +629,7 @@ static KernelChoice choose(int variant, int64_t m, int64_t n, int64_t k, int sm_
     const bool split = kb >= 48 && sp >= 2 && static_cast<double>(t256) / ((full + 1.0) * P) < 0.95;
     tail = split ? 1.0 / sp + 16.0 / kb : 1.0;
   }
-  const double time256 = (full + tail) / 0.87;
+  const double time256 = (full + tail) / 0.907;
   const int64_t t512 = tiles(512);
   const double time512 = static_cast<double>((t512 + P - 1) / P) * 2.0 / 0.96 * (1.0 + 2.0 / kb);
   return time512 < time256 ? KernelChoice{2, 512, true, 8, true} : KernelChoice{2, 256, true, 8, true};
