@@ -47,12 +47,13 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on BASELINE config 0 (4096^3 per GPU)")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--variant", default="tuned")
     ap.add_argument("--no-cublaslt", action="store_true", help="skip the cuBLASLt comparator leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-lowp", action="store_true", help="skip the block-scaled (config 4) section")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -91,7 +92,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.0005):
         self.device_index = device_index
         self.period_s = period_s
         self.samples: list[tuple[int, int]] = []
@@ -135,7 +136,7 @@ class ClockSampler:
                     "note": self.error or "no samples"}
         reasons = sorted({name for _, rs in self.samples for name, bit in self.REASONS.items() if rs & bit})
         return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples), "source": "NVML, 2 ms period"}
+                "reasons": reasons, "samples": len(self.samples), "source": f"NVML, {self.period_s * 1000:g} ms period"}
 
 
 def gpu_index_for(local: int) -> int:
@@ -250,6 +251,87 @@ def run_reference(args, world, rank):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+LOWP_DIM = 8192  # (M, N, K) = (8192, 8192, 8192)
+# Dense tensor rate per clock relative to BF16, measured with the UMMA probe
+# on this pool's B200s (kind::f16 8191, kind::f8f6f4 16381, kind::mxf4nvf4
+# 32762 FLOP/clk/SM for 128 x 256 instructions).
+LOWP_RATE_VS_BF16 = {"fp8_block128": 2.0, "nvfp4": 4.0}
+
+
+def run_lowp(args, stream, flush, peak_bf16: float, peak_kind: str) -> dict:
+    """Block-scaled GEMMs of BASELINE config 4 at 8192^3 on this GPU: the
+    FP8 (128 x 128 FP32 block scales) and NVFP4 (UE4M3 per 16 + FP32 tensor
+    scale) kernels, L2 flushed before every step, checked on sampled rows
+    against the FP32 product of the dequantised inputs."""
+    import torch
+
+    from gb300_microbench_b200 import lowp
+
+    m = n = k = LOWP_DIM
+    flops = 2.0 * m * n * k
+    x, y = lowp.config4_inputs(m, n, k, seed=0, device=stream.device)
+    out = {"workload": "config4_8192x8192x8192", "inputs": "N(0,1) FP32, torch.Generator seed 0, quantised on the GPU",
+           "l2": "flushed before every step", "peak_source": f"{peak_kind} bf16_tflops x measured per-clock rate ratio"}
+
+    def timed(fn, steps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        stream.synchronize()
+        return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+    for kind, op in (("nvfp4", lowp.Nvfp4Operand), ("fp8_block128", lowp.Fp8BlockOperand)):
+        with torch.cuda.stream(stream):
+            a, b = op(x), op(y)
+        stream.synchronize()
+        d = torch.empty(m, n, dtype=torch.bfloat16, device=stream.device)
+        plan = lowp.LowpGemmPlan(kind, a, b, d, stream=stream)
+        plan.run()
+        plan.synchronize()
+        rows = torch.arange(0, m, 61, device=stream.device)
+        with torch.cuda.stream(stream):
+            ref = a.dequantize()[rows].double() @ b.dequantize().double().T
+            err = ((d[rows].double() - ref).norm() / ref.norm()).item()
+        if err > 2e-2:
+            raise SystemExit(f"bench: {kind} GEMM check failed (rel Frobenius {err:.3e} > 2e-2)")
+        del ref
+        plan.run(args.warmup)
+        ms = timed(plan.run, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        plan.run(args.steps)
+        e1.record(stream)
+        stream.synchronize()
+        hot_ms = e0.elapsed_time(e1) / args.steps
+        plan.synchronize()
+        tflops = flops / (ms / 1000.0) / 1e12
+        peak = peak_bf16 * LOWP_RATE_VS_BF16[kind]
+        res = {"tflops": tflops, "ms_per_step": ms, "hot_tflops": flops / (hot_ms / 1000.0) / 1e12,
+               "check_rel_frobenius_sampled_rows": err, "plan": plan.info,
+               "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                            "frac": tflops / peak}}
+        plan.close()
+        if not args.no_cublaslt:
+            d2 = torch.empty_like(d)
+            try:
+                cmp = lowp.CublasLtLowpPlan(kind, a, b, d2, stream=stream)
+                cmp.run(args.warmup)
+                cl_ms = timed(cmp.run, args.steps)
+                res["cublaslt"] = {"tflops": flops / (cl_ms / 1000.0) / 1e12, "ms_per_step": cl_ms,
+                                   "ratio_ours_vs_cublaslt": cl_ms / ms, "version": cmp.info["cublaslt_version"]}
+                cmp.close()
+            except Exception as exc:  # the library has no algorithm for this scaling mode
+                res["cublaslt"] = {"unavailable": str(exc).splitlines()[0][:200]}
+            del d2
+        out[kind] = res
+        del a, b, d
+    return out
 
 
 def run_ours(args, world, rank, local):
@@ -377,6 +459,12 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_matmul_sample()
 
+    # Config 4 (block-scaled FP8 / NVFP4), single-GPU runs only.
+    lowp_res = None
+    if world == 1 and not args.no_lowp:
+        del a_h, b_h, c_h, a_d, b_d, c_d
+        lowp_res = run_lowp(args, stream, flush, peak, pk_kind)
+
     if rank == 0:
         line = {
             "metric": "bf16_gemm_tflops_per_gpu", "value": value, "unit": "TFLOP/s", "n_gpus": world,
@@ -399,6 +487,7 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "clocks": clocks,
             "check": {"rel_frobenius_rows_0_256": err},
+            "lowp_config4": lowp_res,
         }
         print(json.dumps(line), flush=True)
     plan.close()
