@@ -29,7 +29,8 @@
 //               box for A's 128-row block, one 4 KiB box for B's 256 rows).
 //   warp 1      TMEM allocation (512 columns) and the single MMA thread.
 //   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column
-//               half (w - 2) / 4, converts to BF16 and stores D directly.
+//               half (w - 2) / 4, converts to BF16, stages 32 x 64 boxes
+//               with the 128-byte swizzle and writes them with TMA stores.
 //
 // Every wait is bounded (globaltimer budget); a timeout records a status
 // code, drains what is in flight and returns.
@@ -39,6 +40,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <new>
+#include <type_traits>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -77,24 +79,38 @@ struct Cfg {
   static constexpr int SFA_BYTES = kKind == kNvfp4 ? MMAS * SF_ATOM : 0;      // one row block
   static constexpr int SFB_BYTES = kKind == kNvfp4 ? 2 * MMAS * SF_ATOM : 0;  // two row blocks
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES) / STAGE_BYTES;
+  // Epilogue staging: per epilogue warp EPI_BOXES boxes of 32 rows x 128
+  // bytes (64 BF16 columns), written to D by TMA stores. Two per warp for
+  // the CTA pair (its ring is smaller), one otherwise.
+  static constexpr int EPI_BOXES = kCG == 2 ? 2 : 1;
+  static constexpr int EPI_BOX_BYTES = 32 * 128;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BOXES * EPI_BOX_BYTES;
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
   // NVFP4 keeps one TMEM scale area (48 columns) per stage next to the
   // 256-column accumulator.
   static constexpr int STAGES_MAX = kKind == kNvfp4 ? 5 : 8;
   static constexpr int STAGES = STAGES_FIT < STAGES_MAX ? STAGES_FIT : STAGES_MAX;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(STAGES >= 3, "ring too shallow");
+  static_assert((2 * STAGES + 8) * 8 <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
   static_assert(MMAS * 32 == ROW_BYTES, "one instruction consumes 32 bytes of each row");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
 };
 
-// NVFP4 TMEM map: accumulator columns [0, 256); per stage s a scale area at
-// 256 + 48 s: SFA of instruction g at +4g (4 columns), SFB at +16 + 8g
-// (8 columns: two 128-row atoms). FP8 TMEM map: partial buffer b at 256 b.
-constexpr uint32_t kSfBase = 256;
-constexpr uint32_t kSfStageCols = 48;
-static_assert(kSfBase + Cfg<kNvfp4, 1>::STAGES * kSfStageCols <= TMEM_COLS, "TMEM scale ring");
-static_assert(kSfBase + Cfg<kNvfp4, 2>::STAGES * kSfStageCols <= TMEM_COLS, "TMEM scale ring");
+// NVFP4 TMEM map: two overlapping accumulators, tile j in buffer j % 2 at
+// columns [192 b, 192 b + 256): they share one 64-column subtile, which the
+// epilogue drains first, so the next tile's MMAs start while the other 192
+// columns of the previous tile are still being read. One 48-column scale
+// area at 448 (SFA of instruction g at +4g, SFB at +16 + 8g: two 128-row
+// atoms), rewritten every stage: scale copies and MMAs of the issuing thread
+// execute in issue order, so a copy never overtakes the MMA that reads the
+// previous stage's scales. FP8 TMEM map: partial buffer b at 256 b.
+constexpr uint32_t kAccStride = 192;     // NVFP4 accumulator b at column 192 b
+constexpr uint32_t kOverlapCols = 64;    // columns shared by the two accumulators
+constexpr uint32_t kSfBase = 448;
+static_assert(kAccStride + 256 <= kSfBase && kSfBase + 48 <= TMEM_COLS, "NVFP4 TMEM map");
+static_assert(kAccStride + kOverlapCols == 256, "accumulators overlap by one 64-column subtile");
 
 struct Params {
   int32_t m, n, k;
@@ -215,28 +231,6 @@ __device__ __forceinline__ void pack32(const float* v, float s, uint32_t* out) {
   for (int j = 0; j < 16; ++j) out[j] = pack_bf16x2(v[2 * j] * s, v[2 * j + 1] * s);
 }
 
-// Stores one row segment of 128 BF16 (64 packed words) at (row, col0).
-__device__ __forceinline__ void store_row(const Params& p, int row, int col0, const uint32_t (&pk)[64]) {
-  if (row >= p.m) return;
-  __nv_bfloat16* dst = p.d + static_cast<int64_t>(row) * p.n + col0;
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const int col = col0 + 8 * c;
-    if (col + 8 <= p.n) {
-      *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (col + e < p.n) {
-          const uint32_t w = pk[4 * c + e / 2];
-          const uint16_t bits = static_cast<uint16_t>((e & 1) ? (w >> 16) : (w & 0xFFFFu));
-          reinterpret_cast<uint16_t*>(dst)[8 * c + e] = bits;
-        }
-      }
-    }
-  }
-}
-
 // FP32 promotion acc += v * s for 32 values, two lanes per instruction
 // (packed fma.rn.f32x2 of sm_100).
 __device__ __forceinline__ void promote32(float* acc, const uint32_t (&v)[32], float s) {
@@ -255,7 +249,7 @@ template <int kKind, int kCG>
 __global__ void __launch_bounds__(THREADS, 1)
     bb_lowp_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
-                        const Params p) {
+                        const __grid_constant__ CUtensorMap tm_d, const Params p) {
   using C = Cfg<kKind, kCG>;
   constexpr int STAGES = C::STAGES;
   constexpr bool kPair = kCG == 2;
@@ -270,13 +264,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem_b = smem_a + STAGES * C::A_BYTES;
   uint8_t* smem_sfa = smem_b + STAGES * C::B_BYTES;        // NVFP4 only
   uint8_t* smem_sfb = smem_sfa + STAGES * C::SFA_BYTES;    // NVFP4 only
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* smem_epi = smem + STAGES * C::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + C::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;       // [2]
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2], in the leader CTA
-  uint64_t* mma_done = bars + 2 * STAGES + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2], in the leader CTA: buffer fully drained
+  uint64_t* ovl_free = bars + 2 * STAGES + 4;   // [2], in the leader CTA: NVFP4 shared subtile drained
+  uint64_t* mma_done = bars + 2 * STAGES + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -285,6 +281,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_d);
     if constexpr (kKind == kNvfp4) {
       prefetch_tmap(&tm_sfa);
       prefetch_tmap(&tm_sfb);
@@ -298,6 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), EPI_WARPS * kCG);
+      mbar_init(smem_u32(&ovl_free[b]), (EPI_WARPS / 2) * kCG);
     }
     mbar_init(smem_u32(mma_done), 1);
     fence_mbarrier_init_cluster();
@@ -386,15 +384,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         if constexpr (kPair) umma_commit<kCG>(mapa_shared(a, 1));
       };
       for (int t = cluster_idx; ok && t < p.num_tiles; t += p.num_clusters) {
+        uint32_t acc_col = 0;
         if constexpr (kKind == kNvfp4) {
-          if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[0]), (acc_iter & 1u) ^ 1u, p.status, kDevTimeoutMma)) {
+          // Tile j goes to buffer j % 2: wait until tile j - 2 left it, and
+          // until tile j - 1 (the other buffer) drained the shared subtile.
+          const uint32_t b = acc_iter & 1u;
+          if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[b]), ((acc_iter >> 1) & 1u) ^ 1u, p.status,
+                                   kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          if (acc_iter > 0 && !bb_wait_warp<kPair>(smem_u32(&ovl_free[b ^ 1u]), ((acc_iter - 1) >> 1) & 1u,
+                                                   p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          acc_col = b * kAccStride;
         }
         for (int ks = 0; ks < p.k_stages; ++ks) {
-          uint32_t d_tmem = tmem_base;
+          uint32_t d_tmem = tmem_base + acc_col;
           uint32_t buf = 0;
           if constexpr (kKind == kFp8Block) {
             buf = acc_iter & 1u;
@@ -415,7 +424,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * (C::A_BYTES >> 4);
             const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * (C::B_BYTES >> 4);
             if constexpr (kKind == kNvfp4) {
-              const uint32_t sf_cols = sf_cols0 + stage * kSfStageCols;
+              const uint32_t sf_cols = sf_cols0;
               const uint64_t sfa_desc = sfa_desc0 + static_cast<uint64_t>(stage) * (C::SFA_BYTES >> 4);
               const uint64_t sfb_desc = sfb_desc0 + static_cast<uint64_t>(stage) * (C::SFB_BYTES >> 4);
               constexpr uint32_t idesc = idesc_nvf4(C::TILE_M, C::TILE_N);
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         if constexpr (kKind == kNvfp4) {
-          if (elect_one()) commit_both(&acc_full[0]);
+          if (elect_one()) commit_both(&acc_full[acc_iter & 1u]);
           __syncwarp();
           ++acc_iter;
         }
@@ -464,15 +473,46 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     uint32_t acc_iter = 0;
     bool ok = true;
-    auto release = [&](uint32_t buf) {
+    // One arrival per warp on a barrier of the leader CTA, after this
+    // warp's TMEM reads completed.
+    auto arrive_leader = [&](uint64_t* bar) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        const uint32_t eb = smem_u32(&acc_empty[buf]);
+        const uint32_t eb = smem_u32(bar);
         if constexpr (kPair) {
           mbar_arrive_cluster(mapa_shared(eb, 0));
         } else {
           mbar_arrive(eb);
+        }
+      }
+    };
+    auto release = [&](uint32_t buf) { arrive_leader(&acc_empty[buf]); };
+    // D rows row0 .. row0 + 31 (lane = row), columns col0 .. col0 + 127 as two
+    // 32 x 64 boxes: each staged with the 128-byte swizzle in this warp's
+    // boxes of shared memory and written by one TMA store (clipped at the
+    // edges of D; boxes wholly outside D are skipped).
+    const uint32_t ebuf = smem_u32(smem_epi + (warp - 2) * C::EPI_BOXES * C::EPI_BOX_BYTES);
+    uint32_t box_seq = 0;
+    const uint64_t d_policy = l2_policy_evict_first();
+    auto store_boxes = [&](int row0, int col0_, const uint32_t(&pk_)[64]) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t buf = ebuf + (box_seq % C::EPI_BOXES) * C::EPI_BOX_BYTES;
+        ++box_seq;
+        if (lane == 0) bulk_wait_group_read<C::EPI_BOXES - 1>();
+        __syncwarp();
+        const uint32_t row_addr = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pk_[32 * h + 4 * j], pk_[32 * h + 4 * j + 1],
+                       pk_[32 * h + 4 * j + 2], pk_[32 * h + 4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // D is written once: evict-first in L2.
+          if (row0 < p.m && col0_ + 64 * h < p.n) tma_store_2d_hint(&tm_d, buf, col0_ + 64 * h, row0, d_policy);
+          bulk_commit_group();
         }
       }
     };
@@ -483,19 +523,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int col0 = n_blk * C::TILE_N + half * 128;
       uint32_t pk[64];
       if constexpr (kKind == kNvfp4) {
-        if (!bb_wait_warp<kPair>(smem_u32(&acc_full[0]), acc_iter & 1u, p.status, kDevTimeoutEpilogue)) break;
+        const uint32_t b = acc_iter & 1u;
+        if (!bb_wait_warp<kPair>(smem_u32(&acc_full[b]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) break;
         tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_off + half * 128;
-#pragma unroll
-        for (int c = 0; c < 4; c += 2) {
+        const uint32_t taddr = tmem_base + lane_off + b * kAccStride + half * 128;
+        // The subtile shared with the other buffer is columns [192, 256) of
+        // buffer 0 (this warp's chunks 2, 3 when half == 1) and [0, 64) of
+        // buffer 1 (chunks 0, 1 when half == 0); its owners read it first
+        // and report it drained before reading the rest.
+        const bool owner = (b == 0) ? (half == 1) : (half == 0);
+        // Chunk pair c, c + 1 (32 columns each) into pk; compile-time chunk
+        // indices keep pk in registers.
+        auto drain_pair = [&](auto chunk, bool report) {
+          constexpr int c = decltype(chunk)::value;
           uint32_t r0[32], r1[32];
           tmem_ld_32x32b_x32(taddr + 32 * c, r0);
           tmem_ld_32x32b_x32(taddr + 32 * (c + 1), r1);
           tmem_ld_wait();
+          if (report) arrive_leader(&ovl_free[b]);
           pack32(reinterpret_cast<const float*>(r0), p.global_scale, pk + 16 * c);
           pack32(reinterpret_cast<const float*>(r1), p.global_scale, pk + 16 * (c + 1));
+        };
+        if (b == 0) {
+          drain_pair(std::integral_constant<int, 2>{}, owner);
+          drain_pair(std::integral_constant<int, 0>{}, false);
+        } else {
+          drain_pair(std::integral_constant<int, 0>{}, owner);
+          drain_pair(std::integral_constant<int, 2>{}, false);
         }
-        release(0);
+        release(b);
         ++acc_iter;
       } else {
         const float* sa = reinterpret_cast<const float*>(p.sfa);
@@ -534,8 +590,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) pack32(acc + 32 * c, p.global_scale, pk + 16 * c);
       }
-      store_row(p, row, col0, pk);
+      store_boxes(row - lane, col0, pk);
     }
+    if (lane == 0) bulk_wait_group<0>();  // stores read their staging boxes before exit
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -557,7 +615,7 @@ struct bb_lowp_plan {
   int stages = 0;
   int64_t m = 0, n = 0, k = 0;
   cudaStream_t stream = nullptr;
-  CUtensorMap tm_a{}, tm_b{}, tm_sfa{}, tm_sfb{};
+  CUtensorMap tm_a{}, tm_b{}, tm_sfa{}, tm_sfb{}, tm_d{};
   bb::lowp::Params params{};
   int grid = 0;
   int smem_bytes = 0;
@@ -604,7 +662,7 @@ int launch_kind(const bb_lowp_plan& pl) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = launch_config<kKind, kCG>(pl, attr);
   return check_cuda(cudaLaunchKernelEx(&cfg, bb_lowp_gemm_kernel<kKind, kCG>, pl.tm_a, pl.tm_b, pl.tm_sfa, pl.tm_sfb,
-                                       pl.params),
+                                       pl.tm_d, pl.params),
                     "launch bb_lowp_gemm_kernel");
 }
 
@@ -766,6 +824,15 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     } else {
       h->tm_sfa = h->tm_a;  // unused by the FP8 kernel
       h->tm_sfb = h->tm_b;
+    }
+    if (rc == BB_OK) {
+      // D (M x N BF16, row-major) for the epilogue's TMA stores: boxes of 64
+      // columns (128 bytes) x 32 rows, 128-byte swizzle.
+      const uint64_t dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(m)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(n) * 2};
+      const uint32_t box[2] = {64, 32};
+      rc = encode_tiled(&h->tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 2, d, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     }
     if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
     if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
