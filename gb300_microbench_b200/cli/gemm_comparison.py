@@ -371,6 +371,10 @@ def build_rows(mode: str, shape_index: int, mnkl, results, comparison, prov, war
     m, n, k, l = mnkl
     for ci, (res, cmpf) in enumerate(zip(results, comparison)):
         method, variant, scheduler, tile, cluster, two_cta, persistent = res["spec"]
+        if variant == "tuned" and "info" in res:
+            # The tuned slot's tile is chosen per shape by the plan (256 x 256
+            # or 256 x 512 CTA-pair tiles); record the one it chose.
+            tile = (int(res["info"]["mma_tiler_m"]), int(res["info"]["mma_tiler_n"]))
         row = {f: NOT_APPLICABLE for f in (CUBLASLT_ONLY if method == "cutedsl" else CUTEDSL_ONLY)}
         row.update({
             "schema_version": SCHEMA_VERSION if mode == "reference" else BASELINE_SCHEMA_VERSION,
