@@ -115,6 +115,7 @@ BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_gemm_run_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "bb_gemm_synchronize": (c_int, [c_void_p]),
     "bb_gemm_launches": (c_int64, [c_void_p]),
+    "bb_gemm_plan_set_epilogue": (c_int, [c_void_p, c_float, c_float, c_void_p]),
     "bb_gemm_destroy": (c_int, [c_void_p]),
     "bb_gemm_run_noalloc": (c_int, [c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                                     c_void_p, c_int]),
@@ -164,6 +165,7 @@ CMP_SIGNATURES: dict[str, tuple] = {
                                    c_void_p, POINTER(c_void_p), POINTER(CmpInfo)]),
     "bb_cmp_lowp_plan_create": (c_int, [c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_float, c_void_p, c_int, c_void_p, POINTER(c_void_p), POINTER(CmpInfo)]),
+    "bb_cmp_plan_set_epilogue": (c_int, [c_void_p, c_float, c_float, c_void_p]),
     "bb_cmp_execute_n": (c_int, [c_void_p, c_int]),
     "bb_cmp_destroy": (c_int, [c_void_p]),
 }

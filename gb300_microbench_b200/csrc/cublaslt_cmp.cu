@@ -42,6 +42,7 @@ struct bb_cmp_plan {
   const void* first = nullptr;   // cuBLASLt's "A" operand
   const void* second = nullptr;  // cuBLASLt's "B" operand
   void* d = nullptr;
+  const void* c = nullptr;  // C source of beta * C (nullptr: D itself)
   cudaStream_t stream = nullptr;
   float alpha = 1.0f, beta = 0.0f;
 };
@@ -391,10 +392,22 @@ BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k
   }
 }
 
+BB_CMP_API int bb_cmp_plan_set_epilogue(bb_cmp_plan* p, float alpha, float beta, const void* c_src) {
+  if (!p || (beta != 0.0f && !c_src)) {
+    std::snprintf(g_err, sizeof(g_err), "bb_cmp_plan_set_epilogue: bad argument");
+    return 1;
+  }
+  p->alpha = alpha;
+  p->beta = beta;
+  p->c = beta != 0.0f ? c_src : nullptr;
+  return 0;
+}
+
 BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* p, int iterations) {
   if (!p) return 1;
+  const void* c = p->c ? p->c : p->d;
   for (int i = 0; i < iterations; ++i) {
-    cublasStatus_t s = cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, p->d,
+    cublasStatus_t s = cublasLtMatmul(p->handle, p->op, &p->alpha, p->first, p->la, p->second, p->lb, &p->beta, c,
                                       p->ld, p->d, p->ld, &p->algo, p->workspace, p->workspace_bytes, p->stream);
     if (s != CUBLAS_STATUS_SUCCESS) {
       set_err("cublasLtMatmul", static_cast<int>(s));

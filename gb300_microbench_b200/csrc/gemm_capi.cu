@@ -238,6 +238,36 @@ BB_API int bb_gemm_run_host(bb_gemm_plan* plan, const void* a_host, const void* 
   }
 }
 
+BB_API int bb_gemm_plan_set_epilogue(bb_gemm_plan* plan, float alpha, float beta, const void* c_src) {
+  using namespace bb;
+  try {
+    clear_error();
+    if (!plan) {
+      set_error("bb_gemm_plan_set_epilogue: null plan");
+      return BB_ERR_ARGUMENT;
+    }
+    gemm::Plan& p = plan->p;
+    if (beta != 0.0f) {
+      if (!c_src) {
+        set_error("bb_gemm_plan_set_epilogue: beta != 0 needs a C source");
+        return BB_ERR_ARGUMENT;
+      }
+      if (reinterpret_cast<uintptr_t>(c_src) % 16 != 0) {
+        set_error("bb_gemm_plan_set_epilogue: the C source must be 16-byte aligned");
+        return BB_ERR_ARGUMENT;
+      }
+    }
+    p.alpha = alpha;
+    p.beta = beta;
+    p.c_src = beta != 0.0f ? c_src : nullptr;
+    p.epi_mode = beta != 0.0f ? 2 : (alpha != 1.0f ? 1 : 0);
+    return BB_OK;
+  } catch (...) {
+    bb::set_error("bb_gemm_plan_set_epilogue: unexpected C++ exception");
+    return BB_ERR_INTERNAL;
+  }
+}
+
 BB_API int64_t bb_gemm_launches(const bb_gemm_plan* plan) { return plan ? plan->p.launches : -1; }
 
 BB_API int bb_gemm_destroy(bb_gemm_plan* plan) {

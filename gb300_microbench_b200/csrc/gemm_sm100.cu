@@ -27,6 +27,7 @@
 // across all tile-columns) so the A rows and B columns a wave touches stay
 // in L2.
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include <cmath>
 #include <cstdlib>
@@ -55,7 +56,68 @@ struct Params {
   float* partials;   // split-tail FP32 partial slices: (parts - 1) tile-sized areas per tail tile and CTA rank
   int* counters;     // two counters (arrived, done) per tail tile and CTA rank
   int* status;
+  // Epilogue D = alpha * acc + beta * Csrc (epi_mode 0: alpha 1, beta 0;
+  // 1: alpha only; 2: alpha and beta). Csrc has the output's dtype and
+  // (L, M, N) row-major layout and may alias the output.
+  int32_t epi_mode;
+  float alpha, beta;
+  const void* c_src;
 };
+
+// alpha * v[j] (+ beta * Csrc[l][row][col + j]) for kCount consecutive
+// columns of one row; Csrc elements past N (or a row past M) read as 0.
+// Fully unrolled so v stays in registers.
+template <bool kOutF32, int kCount>
+__device__ __forceinline__ void apply_epilogue(const Params& p, float (&v)[kCount], int row, int col, int l) {
+  if (p.epi_mode == 0) return;
+#pragma unroll
+  for (int j = 0; j < kCount; ++j) v[j] *= p.alpha;
+  if (p.epi_mode != 2 || row >= p.m) return;
+  const int64_t base = (static_cast<int64_t>(l) * p.m + row) * p.n + col;
+  if constexpr (kOutF32) {
+    const float* c = static_cast<const float*>(p.c_src) + base;
+#pragma unroll
+    for (int j = 0; j < kCount; j += 4) {
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (col + j + 4 <= p.n) {
+        const float4 q4 = __ldg(reinterpret_cast<const float4*>(c + j));
+        x[0] = q4.x;
+        x[1] = q4.y;
+        x[2] = q4.z;
+        x[3] = q4.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (col + j + e < p.n) x[e] = __ldg(c + j + e);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[j + e] = fmaf(p.beta, x[e], v[j + e]);
+    }
+  } else {
+    const __nv_bfloat16* c = static_cast<const __nv_bfloat16*>(p.c_src) + base;
+#pragma unroll
+    for (int j = 0; j < kCount; j += 8) {
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (col + j + 8 <= p.n) {
+        const uint4 q4 = __ldg(reinterpret_cast<const uint4*>(c + j));
+        w[0] = q4.x;
+        w[1] = q4.y;
+        w[2] = q4.z;
+        w[3] = q4.w;
+      } else {
+        const uint16_t* c16 = reinterpret_cast<const uint16_t*>(c + j);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (col + j + e < p.n) w[e / 2] |= static_cast<uint32_t>(__ldg(c16 + e)) << (16 * (e & 1));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[j + 2 * e] = fmaf(p.beta, __uint_as_float(w[e] << 16), v[j + 2 * e]);
+        v[j + 2 * e + 1] = fmaf(p.beta, __uint_as_float(w[e] & 0xFFFF0000u), v[j + 2 * e + 1]);
+      }
+    }
+  }
+}
 
 struct WorkItem {
   int tile;
@@ -436,6 +498,14 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
             uint32_t r0[32];
             tmem_ld_32x32b_x32(t_row + wc0 + h * 32, r0);
             tmem_ld_wait();
+            if (p.epi_mode != 0) {
+              float v[32];
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) v[jj] = __uint_as_float(r0[jj]);
+              apply_epilogue<kOutF32, 32>(p, v, row0 + lane, n_blk * kBN + wc0 + h * 32, l);
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) r0[jj] = __float_as_uint(v[jj]);
+            }
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj)
               pk[h / 2][(h & 1) * 16 + jj] = pack_bf16x2(__uint_as_float(r0[2 * jj]), __uint_as_float(r0[2 * jj + 1]));
@@ -464,6 +534,7 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) v[jj] = __uint_as_float(r0[jj]);
             if (c == kWarpChunks - 1) release_acc(acc);  // accumulator now lives in registers
+            apply_epilogue<kOutF32, ncols>(p, *reinterpret_cast<float(*)[ncols]>(v), row0 + lane, n_blk * kBN + col, l);
             uint32_t packed[32];
             pack_chunk(v, packed);
             store_chunk(packed, row0, n_blk * kBN + col, l);
@@ -557,6 +628,8 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
                 v[4 * jj + 3] += x[jj].w;
               }
             }
+            apply_epilogue<kOutF32, ncols>(p, *reinterpret_cast<float(*)[ncols]>(v), row0 + lane,
+                                           n_blk * kBN + c * C::EPI_COLS, l);
             uint32_t packed[32];
             pack_chunk(v, packed);
             store_chunk(packed, row0, n_blk * kBN + c * C::EPI_COLS, l);
@@ -669,6 +742,10 @@ static int launch(const Plan& pl) {
   prm.partials = pl.partials;
   prm.counters = pl.counters;
   prm.status = pl.status;
+  prm.epi_mode = pl.epi_mode;
+  prm.alpha = pl.alpha;
+  prm.beta = pl.beta;
+  prm.c_src = pl.c_src;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, pl.tm_a, pl.tm_b, pl.tm_c, prm), "cudaLaunchKernelEx(gemm)");
 }
 

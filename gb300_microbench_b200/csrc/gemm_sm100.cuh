@@ -32,6 +32,10 @@ struct Plan {
   float* partials = nullptr;
   int* counters = nullptr;
   int* status = nullptr;  // device word: 0, or the code of a timed-out wait
+  // Epilogue D = alpha * acc + beta * c_src (bb_gemm_plan_set_epilogue).
+  int epi_mode = 0;
+  float alpha = 1.0f, beta = 0.0f;
+  const void* c_src = nullptr;
   int64_t launches = 0;
   int (*launch)(const Plan&) = nullptr;
 };

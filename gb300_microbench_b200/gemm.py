@@ -96,6 +96,20 @@ class GemmPlan:
         nat.check("bb_gemm_run_host", self._lib.bb_gemm_run_host(
             self._handle, a_host.data_ptr(), b_host.data_ptr(), c_host.data_ptr()))
 
+    def set_epilogue(self, alpha: float = 1.0, beta: float = 0.0, c_src: torch.Tensor | None = None) -> None:
+        """Later launches compute C = alpha * A @ B^T + beta * c_src; c_src has
+        C's shape and dtype (it may be C itself)."""
+        ptr = None
+        if beta != 0.0:
+            if c_src is None:
+                raise ValueError("beta != 0 needs c_src")
+            if c_src.shape != self.c.shape or c_src.dtype != self.c.dtype or not c_src.is_contiguous() or not c_src.is_cuda:
+                raise ValueError("c_src must be a contiguous CUDA tensor with C's shape and dtype")
+            self._c_src = c_src
+            ptr = c_src.data_ptr()
+        nat.check("bb_gemm_plan_set_epilogue", self._lib.bb_gemm_plan_set_epilogue(self._handle, float(alpha),
+                                                                                   float(beta), ptr))
+
     @property
     def launches(self) -> int:
         return int(self._lib.bb_gemm_launches(self._handle))
@@ -158,6 +172,16 @@ class CublasLtPlan:
         self.algo_index = int(info.heuristic_index)
         self.algo_count = int(info.heuristic_returned)
         self.workspace_bytes = int(info.workspace_bytes)
+
+    def set_epilogue(self, alpha: float = 1.0, beta: float = 0.0, c_src: torch.Tensor | None = None) -> None:
+        """Later executions compute D = alpha * A @ B^T + beta * c_src."""
+        if beta != 0.0 and c_src is None:
+            raise ValueError("beta != 0 needs c_src")
+        self._c_src = c_src
+        rc = self._lib.bb_cmp_plan_set_epilogue(self._handle, float(alpha), float(beta),
+                                                c_src.data_ptr() if beta != 0.0 else None)
+        if rc != 0:
+            raise nat.NativeCallError("bb_cmp_plan_set_epilogue", rc, self._lib.bb_cmp_last_error().decode())
 
     def run(self, iterations: int = 1) -> None:
         rc = self._lib.bb_cmp_execute_n(self._handle, int(iterations))

@@ -114,6 +114,14 @@ BB_API int bb_gemm_run_host(bb_gemm_plan* plan, const void* a_host, const void* 
  * recorded by any launch so far (BB_ERR_TIMEOUT) or a CUDA error. Replaces
  * the synchronize step of the reference bridge (cublaslt_bridge.cu:987). */
 BB_API int bb_gemm_synchronize(bb_gemm_plan* plan);
+/* Epilogue of later launches: C = alpha * A * B^T + beta * Csrc, where
+ * Csrc (device pointer) has C's dtype and (L, M, N) row-major layout, is
+ * 16-byte aligned and may be the plan's own C (in-place accumulate). Csrc is
+ * read only when beta != 0 (then it must not be NULL). Defaults: alpha 1,
+ * beta 0. The reference bridge exposes alpha / beta through its cuBLASLt
+ * descriptor (gemm_comparison/cublaslt_bridge.cu:101-128, fixed to 1 / 0
+ * there); this is the same epilogue for the sm_100a kernel. */
+BB_API int bb_gemm_plan_set_epilogue(bb_gemm_plan* plan, float alpha, float beta, const void* c_src);
 /* Number of kernel launches made through this plan so far. */
 BB_API int64_t bb_gemm_launches(const bb_gemm_plan* plan);
 /* Replaces p35_plan_destroy (cublaslt_bridge.cu:1008). */

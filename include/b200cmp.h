@@ -68,6 +68,9 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
 BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const void* a, const void* b,
                                        const void* sfa, const void* sfb, float global_scale, void* d, int autotune,
                                        void* stream, bb_cmp_plan** plan, bb_cmp_info* info);
+/* D = alpha * A * B^T + beta * Csrc for later executions (Csrc: D's dtype
+ * and layout, may be D; read only when beta != 0). */
+BB_CMP_API int bb_cmp_plan_set_epilogue(bb_cmp_plan* plan, float alpha, float beta, const void* c_src);
 BB_CMP_API int bb_cmp_execute_n(bb_cmp_plan* plan, int iterations);
 BB_CMP_API int bb_cmp_destroy(bb_cmp_plan* plan);
 

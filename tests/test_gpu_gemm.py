@@ -190,3 +190,64 @@ def test_tuned_tile_shapes_exact(cuda_device, monkeypatch, tile_n, mnk, force_sp
             assert torch.equal(c, ref)
         else:
             assert torch.equal(c, ref.to(torch.bfloat16))
+
+
+EPI_CASES = [(v, mnk, None) for v in ("tuned", "persistent_1cta", "persistent_2cta")
+             for mnk in ((512, 768, 320), (300, 264, 200), (1024, 1024, 4096))]
+EPI_CASES += [("tuned", (4096, 4096, 4096), None),   # split tail
+              ("tuned", (1024, 1024, 4096), "512")]  # 512-wide tile, eight-warp epilogue
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("variant,mnk,tile_n", EPI_CASES)
+@pytest.mark.parametrize("alpha,beta,inplace", [(0.5, 0.0, False), (1.5, -2.0, False), (1.0, 1.0, True)])
+def test_alpha_beta_epilogue(cuda_device, out_dtype, variant, mnk, tile_n, alpha, beta, inplace, monkeypatch):
+    """C = alpha A B^T + beta Csrc on every store path (whole tiles, the
+    512-wide tile, the split tail), Csrc separate or C itself. Integer
+    operands, FP32 output: exact; BF16 output: within BF16 rounding."""
+    if tile_n:
+        monkeypatch.setenv("BB_GEMM_TILE_N", tile_n)
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0], b[0]
+    g = torch.Generator().manual_seed(7)
+    csrc = torch.randint(-4, 5, (m, n), generator=g).to(out_dtype)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    c = (csrc.clone() if inplace else torch.full((m, n), float("nan"), dtype=out_dtype)).to(cuda_device)
+    src = c if inplace else csrc.to(cuda_device)
+    plan = GemmPlan(ad, bd, c, variant=variant)
+    if tile_n:
+        assert plan.info["mma_tiler_n"] == int(tile_n)
+    plan.set_epilogue(alpha, beta, src if beta != 0.0 else None)
+    plan.run()
+    plan.synchronize()
+    plan.close()
+    prod = oracle.gemm_reference_fp32(a, b)
+    ref = alpha * prod + beta * csrc.float()
+    got = c.float().cpu()
+    if out_dtype == torch.float32:
+        assert torch.equal(got, ref), (got - ref).abs().max()
+    else:
+        err = oracle.rel_frobenius(got, ref)
+        assert err <= 4e-3, err
+
+
+def test_alpha_beta_matches_cublaslt(cuda_device):
+    """The comparator computes the same epilogue on the same operands."""
+    m, n, k = 1024, 768, 512
+    a, b = inputs.reference_mode_operands(m, n, k)
+    ad, bd = a[0].to(cuda_device), b[0].to(cuda_device)
+    csrc = torch.randint(-3, 4, (m, n), generator=torch.Generator().manual_seed(3)).float().to(cuda_device)
+    ours = torch.empty(m, n, dtype=torch.float32, device=cuda_device)
+    theirs = torch.empty_like(ours)
+    plan = GemmPlan(ad, bd, ours, variant="tuned")
+    plan.set_epilogue(0.25, 3.0, csrc)
+    plan.run()
+    plan.synchronize()
+    cmp = CublasLtPlan(ad, bd, theirs, layout="reference")
+    cmp.set_epilogue(0.25, 3.0, csrc)
+    cmp.run()
+    torch.cuda.synchronize()
+    assert torch.equal(ours, theirs)
+    plan.close()
+    cmp.close()
