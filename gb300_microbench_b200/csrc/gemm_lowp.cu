@@ -59,7 +59,10 @@ constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr int BAR_BYTES = 256;
-constexpr int GROUP_M = 8;
+// Grouped raster: group_m tile-rows are swept across all tile-columns. The
+// host sizes a group's A rows to about 32 MiB (a quarter of L2), so a wave's
+// A block stays resident while B streams.
+constexpr int64_t kGroupABytes = 32ll << 20;
 constexpr int SMEM_LIMIT = 232448;
 
 // kCG = 1: one CTA computes a 128 x 256 tile. kCG = 2: a CTA pair computes a
@@ -118,6 +121,7 @@ struct Params {
   int32_t k_stages;    // K / K_PER_STAGE
   int32_t rb_m, rb_n;  // 128-row blocks of A and B
   int32_t num_clusters;
+  int32_t group_m;
   const uint8_t* sfa;  // FP8: FP32 block scales (NVFP4 scales travel by TMA)
   const uint8_t* sfb;
   float global_scale;
@@ -216,10 +220,10 @@ __device__ __forceinline__ void load_2d(uint32_t dst, const void* tmap, uint32_t
 }
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& m_blk, int& n_blk) {
-  const int group_size = GROUP_M * p.tiles_n;
+  const int group_size = p.group_m * p.tiles_n;
   const int g = t / group_size;
-  const int first_m = g * GROUP_M;
-  const int gm = min(GROUP_M, p.tiles_m - first_m);
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first_m);
   const int local = t - g * group_size;
   m_blk = first_m + local % gm;
   n_blk = local / gm;
@@ -570,7 +574,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float s = s_next;
           if (ks + 1 < p.k_stages) s_next = __ldg(sa_row + ks + 1) * __ldg(sb_row + ks + 1);
           const uint32_t buf = acc_iter & 1u;
-          if (!bb_wait_warp<kPair>(smem_u32(&acc_full[buf]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) {
+          // Spin without the suspend hint: this wait is on the per-K-block
+          // MMA -> promotion -> MMA hand-off, where wake-up latency counts.
+          if (!bb_wait_warp<kPair, false>(smem_u32(&acc_full[buf]), (acc_iter >> 1) & 1u, p.status,
+                                          kDevTimeoutEpilogue)) {
             ok = false;
             break;
           }
@@ -700,6 +707,9 @@ void plan_geometry(bb_lowp_plan& h, int sm_count) {
   p.tiles_m = static_cast<int32_t>((h.m + C::TILE_M - 1) / C::TILE_M);
   p.tiles_n = static_cast<int32_t>((h.n + C::TILE_N - 1) / C::TILE_N);
   p.num_tiles = p.tiles_m * p.tiles_n;
+  const int64_t a_tile_bytes = static_cast<int64_t>(C::TILE_M) * (kKind == kNvfp4 ? h.k / 2 : h.k);
+  const int64_t g = kGroupABytes / (a_tile_bytes > 0 ? a_tile_bytes : 1);
+  p.group_m = static_cast<int32_t>(g < 1 ? 1 : (g > p.tiles_m ? p.tiles_m : g));
   const int clusters = max_clusters<kKind, kCG>(h, sm_count);
   p.num_clusters = p.num_tiles < clusters ? p.num_tiles : clusters;
   h.grid = p.num_clusters * kCG;

@@ -203,12 +203,18 @@ __device__ __forceinline__ bool bb_wait(uint32_t addr, uint32_t parity, int* sta
 // around it stay warp-uniform. Issue loops built this way (whole warp waits,
 // one elect.sync lane issues) keep tcgen05 issue well ahead of execution; a
 // lone lane looping inside a divergent branch issues markedly slower.
-template <bool kClusterScope = false>
+// kHint = false polls without the suspend hint (lowest wake-up latency, for
+// waits on the critical path of a tight hand-off).
+template <bool kClusterScope = false, bool kHint = true>
 __device__ __forceinline__ bool bb_wait_warp(uint32_t addr, uint32_t parity, int* status, int code,
                                              bool honor_abort = true, uint64_t budget_ns = kWaitBudgetNs) {
-  constexpr uint32_t kHint = 1000000u;
+  constexpr uint32_t kHintNs = 1000000u;
   auto probe = [&]() {
-    return kClusterScope ? mbar_try_wait_cluster_hint(addr, parity, kHint) : mbar_try_wait_hint(addr, parity, kHint);
+    if constexpr (kHint) {
+      return kClusterScope ? mbar_try_wait_cluster_hint(addr, parity, kHintNs) : mbar_try_wait_hint(addr, parity, kHintNs);
+    } else {
+      return kClusterScope ? mbar_try_wait_cluster(addr, parity) : mbar_try_wait(addr, parity);
+    }
   };
   bool ok = probe();
   if (!ok) {
