@@ -451,8 +451,11 @@ def run_ours(args, world, rank, local):
         eplan.run_host(a_h, b_h, c_h)
         t_e2e.append(time.perf_counter() - t0)
     e2e_s = all_max(world, statistics.mean(t_e2e))
-    if not torch.equal(c_h[:256], c[:256].cpu()):
-        raise SystemExit("bench: end-to-end result differs from the device-path result")
+    # The host path runs row chunks as separate GEMMs (their tiling may
+    # differ from the whole problem's), so it is checked against the oracle.
+    e2e_err = oracle.rel_frobenius(c_h[:256].float(), ref)
+    if e2e_err > 1e-2:
+        raise SystemExit(f"bench: end-to-end result check failed (rel Frobenius {e2e_err:.3e} > 1e-2)")
     h2d = a_h.numel() * 2 + b_h.numel() * 2
     d2h = c_h.numel() * 2
     eplan.close()
@@ -490,7 +493,9 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "e2e": {"value": world * flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1000.0,
-                    "path": "bb_gemm_run_host (pinned host A, B -> device, GEMM, C -> pinned host)"},
+                    "path": "bb_gemm_run_host (pinned host A, B -> device, GEMM, C -> pinned host; B first, then A "
+                            "in row chunks whose GEMMs and C copies overlap the remaining transfers)",
+                    "check_rel_frobenius_rows_0_256": e2e_err},
             "gpu_launches": launches,
             "clocks": clocks,
             "check": {"rel_frobenius_rows_0_256": err},

@@ -11,9 +11,26 @@ namespace bb {
 std::atomic<int64_t> g_kernel_launches{0};
 }
 
+// Host-buffer pipeline of bb_gemm_run_host: B first, then A in row chunks
+// on an H2D stream; each chunk's GEMM on the plan's stream once its rows have
+// landed; its C rows back on a D2H stream while later A chunks still arrive,
+// so both copy directions and the compute overlap.
+constexpr int kPipeChunks = 4;
+
+struct HostPipe {
+  static constexpr int kMaxChunks = 8;
+  bool ready = false;
+  int chunks = 0;
+  int64_t row0[kMaxChunks] = {}, rows[kMaxChunks] = {};
+  bb::gemm::Plan sub[kMaxChunks];
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_b = nullptr, ev_a[kMaxChunks] = {}, ev_c[kMaxChunks] = {};
+};
+
 struct bb_gemm_plan {
   bb::gemm::Plan p;
   int* status_dev = nullptr;
+  HostPipe pipe;
 };
 
 namespace bb {
@@ -75,6 +92,87 @@ void fill_info(const bb::gemm::Plan& p, bb_gemm_info* info) {
   info->raster_group_m = p.group_m;
   info->c_dtype = p.c_dtype;
   info->variant = p.variant;
+}
+
+void free_pipe(HostPipe& hp) {
+  for (int i = 0; i < HostPipe::kMaxChunks; ++i) {
+    if (hp.sub[i].partials) cudaFree(hp.sub[i].partials);
+    if (hp.sub[i].counters) cudaFree(hp.sub[i].counters);
+    hp.sub[i].partials = nullptr;
+    hp.sub[i].counters = nullptr;
+    if (hp.ev_a[i]) cudaEventDestroy(hp.ev_a[i]);
+    if (hp.ev_c[i]) cudaEventDestroy(hp.ev_c[i]);
+    hp.ev_a[i] = hp.ev_c[i] = nullptr;
+  }
+  if (hp.ev_b) cudaEventDestroy(hp.ev_b);
+  if (hp.h2d) cudaStreamDestroy(hp.h2d);
+  if (hp.d2h) cudaStreamDestroy(hp.d2h);
+  hp.ev_b = nullptr;
+  hp.h2d = hp.d2h = nullptr;
+  hp.ready = false;
+}
+
+// Sub-plans over row chunks of a single-batch plan (chunk rows are multiples
+// of 256, the CTA-pair tile height), their workspaces, streams and events.
+int init_pipe(bb_gemm_plan* plan) {
+  using namespace bb;
+  HostPipe& hp = plan->pipe;
+  const gemm::Plan& p = plan->p;
+  DeviceInfo dev;
+  int rc = query_device(&dev);
+  if (rc != BB_OK) return rc;
+  const int64_t units = p.m / 256;  // whole 256-row blocks
+  // Four chunks measured best at 4096^3 (e2e 86.9 TFLOP/s; eight: 83.0, the
+  // per-copy and per-launch costs outweigh the shorter tail).
+  int chunks = static_cast<int>(units < kPipeChunks ? units : kPipeChunks);
+  if (chunks < 2) return BB_ERR_UNSUPPORTED;
+  hp.chunks = chunks;
+  const size_t es = p.c_dtype == BB_DTYPE_F32 ? 4 : 2;
+  int64_t r = 0;
+  for (int i = 0; i < chunks; ++i) {
+    const int64_t rows = (i == chunks - 1) ? p.m - r : ((units * (i + 1)) / chunks - (units * i) / chunks) * 256;
+    hp.row0[i] = r;
+    hp.rows[i] = rows;
+    gemm::Plan& q = hp.sub[i];
+    q = gemm::Plan{};
+    q.m = rows;
+    q.n = p.n;
+    q.k = p.k;
+    q.l = 1;
+    q.a = static_cast<const uint8_t*>(p.a) + static_cast<size_t>(r) * p.k * 2;
+    q.b = p.b;
+    q.c = static_cast<uint8_t*>(p.c) + static_cast<size_t>(r) * p.n * es;
+    q.c_dtype = p.c_dtype;
+    q.stream = p.stream;
+    q.alpha = p.alpha;
+    q.beta = p.beta;
+    q.epi_mode = p.epi_mode;
+    q.c_src = p.c_src ? static_cast<const uint8_t*>(p.c_src) + static_cast<size_t>(r) * p.n * es : nullptr;
+    rc = gemm::plan_init(q, p.variant, dev.sm_count);
+    if (rc == BB_OK) rc = gemm::build_maps(q);
+    if (rc == BB_OK && q.sk_parts > 0) {
+      rc = check_cuda(cudaMalloc(&q.partials, q.partial_floats * sizeof(float)), "cudaMalloc(pipe partials)");
+      if (rc == BB_OK) rc = check_cuda(cudaMalloc(&q.counters, q.counter_ints * sizeof(int)), "cudaMalloc(pipe counters)");
+      if (rc == BB_OK) rc = check_cuda(cudaMemset(q.counters, 0, q.counter_ints * sizeof(int)), "cudaMemset(pipe counters)");
+    }
+    q.status = plan->status_dev;
+    if (rc == BB_OK) rc = check_cuda(cudaEventCreateWithFlags(&hp.ev_a[i], cudaEventDisableTiming), "cudaEventCreate");
+    if (rc == BB_OK) rc = check_cuda(cudaEventCreateWithFlags(&hp.ev_c[i], cudaEventDisableTiming), "cudaEventCreate");
+    if (rc != BB_OK) {
+      free_pipe(hp);
+      return rc;
+    }
+    r += rows;
+  }
+  rc = check_cuda(cudaEventCreateWithFlags(&hp.ev_b, cudaEventDisableTiming), "cudaEventCreate");
+  if (rc == BB_OK) rc = check_cuda(cudaStreamCreateWithFlags(&hp.h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc == BB_OK) rc = check_cuda(cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc != BB_OK) {
+    free_pipe(hp);
+    return rc;
+  }
+  hp.ready = true;
+  return BB_OK;
 }
 
 }  // namespace
@@ -223,14 +321,52 @@ BB_API int bb_gemm_run_host(bb_gemm_plan* plan, const void* a_host, const void* 
       return BB_ERR_ARGUMENT;
     }
     gemm::Plan& p = plan->p;
+    const size_t es = p.c_dtype == BB_DTYPE_F32 ? 4 : 2;
     const size_t a_bytes = static_cast<size_t>(p.m) * p.k * p.l * 2;
     const size_t b_bytes = static_cast<size_t>(p.n) * p.k * p.l * 2;
-    const size_t c_bytes = static_cast<size_t>(p.m) * p.n * p.l * (p.c_dtype == BB_DTYPE_F32 ? 4 : 2);
-    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.a), a_host, a_bytes, cudaMemcpyHostToDevice, p.stream));
-    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, p.stream));
-    int rc = bb_gemm_execute_n(plan, 1);
-    if (rc != BB_OK) return rc;
-    BB_CUDA_TRY(cudaMemcpyAsync(c_host, p.c, c_bytes, cudaMemcpyDeviceToHost, p.stream));
+    const size_t c_bytes = static_cast<size_t>(p.m) * p.n * p.l * es;
+    HostPipe& hp = plan->pipe;
+    if (p.l == 1 && p.m >= 512 && !hp.ready) {
+      const int rc = init_pipe(plan);
+      if (rc != BB_OK && rc != BB_ERR_UNSUPPORTED) return rc;
+    }
+    if (!hp.ready || p.epi_mode != hp.sub[0].epi_mode || p.alpha != hp.sub[0].alpha || p.beta != hp.sub[0].beta) {
+      // Serial path (batched problems, few rows, or an epilogue changed
+      // since the pipeline was built).
+      BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.a), a_host, a_bytes, cudaMemcpyHostToDevice, p.stream));
+      BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, p.stream));
+      int rc = bb_gemm_execute_n(plan, 1);
+      if (rc != BB_OK) return rc;
+      BB_CUDA_TRY(cudaMemcpyAsync(c_host, p.c, c_bytes, cudaMemcpyDeviceToHost, p.stream));
+      return bb_gemm_synchronize(plan);
+    }
+    // Pipelined path. Work queued earlier on the plan's stream finishes
+    // before the copies overwrite A and B.
+    BB_CUDA_TRY(cudaEventRecord(hp.ev_b, p.stream));
+    BB_CUDA_TRY(cudaStreamWaitEvent(hp.h2d, hp.ev_b, 0));
+    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, hp.h2d));
+    BB_CUDA_TRY(cudaEventRecord(hp.ev_b, hp.h2d));
+    for (int i = 0; i < hp.chunks; ++i) {
+      const size_t off = static_cast<size_t>(hp.row0[i]) * p.k * 2;
+      BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(const_cast<void*>(p.a)) + off,
+                                  static_cast<const uint8_t*>(a_host) + off, static_cast<size_t>(hp.rows[i]) * p.k * 2,
+                                  cudaMemcpyHostToDevice, hp.h2d));
+      BB_CUDA_TRY(cudaEventRecord(hp.ev_a[i], hp.h2d));
+    }
+    BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_b, 0));
+    for (int i = 0; i < hp.chunks; ++i) {
+      BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_a[i], 0));
+      int rc = hp.sub[i].launch(hp.sub[i]);
+      if (rc != BB_OK) return rc;
+      ++p.launches;
+      g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+      BB_CUDA_TRY(cudaEventRecord(hp.ev_c[i], p.stream));
+      BB_CUDA_TRY(cudaStreamWaitEvent(hp.d2h, hp.ev_c[i], 0));
+      const size_t coff = static_cast<size_t>(hp.row0[i]) * p.n * es;
+      BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(c_host) + coff, static_cast<const uint8_t*>(p.c) + coff,
+                                  static_cast<size_t>(hp.rows[i]) * p.n * es, cudaMemcpyDeviceToHost, hp.d2h));
+    }
+    BB_CUDA_TRY(cudaStreamSynchronize(hp.d2h));
     return bb_gemm_synchronize(plan);
   } catch (...) {
     bb::set_error("bb_gemm_run_host: unexpected C++ exception");
@@ -261,6 +397,16 @@ BB_API int bb_gemm_plan_set_epilogue(bb_gemm_plan* plan, float alpha, float beta
     p.beta = beta;
     p.c_src = beta != 0.0f ? c_src : nullptr;
     p.epi_mode = beta != 0.0f ? 2 : (alpha != 1.0f ? 1 : 0);
+    // The host-buffer pipeline's row-chunk plans follow.
+    HostPipe& hp = plan->pipe;
+    const size_t es = p.c_dtype == BB_DTYPE_F32 ? 4 : 2;
+    for (int i = 0; hp.ready && i < hp.chunks; ++i) {
+      hp.sub[i].alpha = p.alpha;
+      hp.sub[i].beta = p.beta;
+      hp.sub[i].epi_mode = p.epi_mode;
+      hp.sub[i].c_src =
+          p.c_src ? static_cast<const uint8_t*>(p.c_src) + static_cast<size_t>(hp.row0[i]) * p.n * es : nullptr;
+    }
     return BB_OK;
   } catch (...) {
     bb::set_error("bb_gemm_plan_set_epilogue: unexpected C++ exception");
@@ -274,6 +420,7 @@ BB_API int bb_gemm_destroy(bb_gemm_plan* plan) {
   using namespace bb;
   if (!plan) return BB_OK;
   int rc = BB_OK;
+  free_pipe(plan->pipe);
   for (void* ptr : {static_cast<void*>(plan->status_dev), static_cast<void*>(plan->p.partials),
                     static_cast<void*>(plan->p.counters)}) {
     if (!ptr) continue;

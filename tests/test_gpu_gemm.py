@@ -115,6 +115,33 @@ def test_run_host_matches_device_path(cuda_device):
     assert torch.equal(c_host, ref)
 
 
+@pytest.mark.parametrize("mnk,dtype", [((4096, 1024, 2048), torch.bfloat16), ((1280, 520, 264), torch.float32)])
+def test_run_host_pipelined(cuda_device, mnk, dtype):
+    """Host-buffer path with the row-chunk pipeline (B first, A chunks, each
+    chunk's GEMM and C copy overlapping later transfers): integer operands,
+    so every tiling gives the exact product."""
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0].contiguous(), b[0].contiguous()
+    ad = torch.empty_like(a, device=cuda_device)
+    bd = torch.empty_like(b, device=cuda_device)
+    c = torch.empty(m, n, dtype=dtype, device=cuda_device)
+    plan = GemmPlan(ad, bd, c)
+    c_host = torch.full((m, n), float("nan"), dtype=dtype).pin_memory()
+    for _ in range(2):  # the second call reuses the pipeline
+        plan.run_host(a.pin_memory(), b.pin_memory(), c_host)
+    ref = oracle.gemm_reference_fp32(a, b)
+    if dtype == torch.float32:
+        assert torch.equal(c_host, ref)
+    else:
+        assert oracle.rel_frobenius(c_host.float(), ref) < 4e-3
+    plan.set_epilogue(2.0, 0.0)
+    plan.run_host(a.pin_memory(), b.pin_memory(), c_host)
+    if dtype == torch.float32:
+        assert torch.equal(c_host, 2.0 * ref)
+    plan.close()
+
+
 def test_cublaslt_comparator_agrees(cuda_device):
     a, b = inputs.baseline_mode_operands(1024, 1024, 1024)
     ad, bd = a.to(cuda_device), b.to(cuda_device)
