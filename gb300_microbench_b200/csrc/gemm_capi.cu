@@ -2,6 +2,8 @@
 // Mirrors the plan life cycle of the reference's cuBLASLt bridge
 // (gemm_comparison/cublaslt_bridge.cu:563-1016) for our own kernel.
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <new>
 
 #include "common.cuh"
@@ -124,13 +126,32 @@ int init_pipe(bb_gemm_plan* plan) {
   const int64_t units = p.m / 256;  // whole 256-row blocks
   // Four chunks measured best at 4096^3 (e2e 86.9 TFLOP/s; eight: 83.0, the
   // per-copy and per-launch costs outweigh the shorter tail).
-  int chunks = static_cast<int>(units < kPipeChunks ? units : kPipeChunks);
+  int want = kPipeChunks;
+  bool taper = false;  // 1:3:3:1 row weights (four chunks)
+  // BB_GEMM_PIPE=<chunks>[t] overrides (t: tapered four-chunk weights).
+  if (const char* env = std::getenv("BB_GEMM_PIPE")) {
+    const int c = std::atoi(env);
+    if (c >= 1 && c <= HostPipe::kMaxChunks) want = c;
+    taper = std::strchr(env, 't') != nullptr;
+  }
+  int chunks = static_cast<int>(units < want ? units : want);
   if (chunks < 2) return BB_ERR_UNSUPPORTED;
   hp.chunks = chunks;
   const size_t es = p.c_dtype == BB_DTYPE_F32 ? 4 : 2;
   int64_t r = 0;
+  // Row weights 1:3:3:1 for four chunks: a small first chunk starts the
+  // D2H stream early, a small last one shortens the tail after the final
+  // H2D byte (its GEMM and C copy); the middle chunks carry the bulk.
+  static const int kWeights4[4] = {1, 3, 3, 1};
+  int64_t bounds[HostPipe::kMaxChunks + 1] = {0};
+  for (int i = 0, acc = 0; i < chunks; ++i) {
+    const bool tw = taper && chunks == 4 && units >= 8;
+    acc += tw ? kWeights4[i] : 1;
+    const int total = tw ? 8 : chunks;
+    bounds[i + 1] = (units * acc) / total;
+  }
   for (int i = 0; i < chunks; ++i) {
-    const int64_t rows = (i == chunks - 1) ? p.m - r : ((units * (i + 1)) / chunks - (units * i) / chunks) * 256;
+    const int64_t rows = (i == chunks - 1) ? p.m - r : (bounds[i + 1] - bounds[i]) * 256;
     hp.row0[i] = r;
     hp.rows[i] = rows;
     gemm::Plan& q = hp.sub[i];
