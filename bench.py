@@ -328,6 +328,19 @@ def run_lowp(args, stream, flush, peak_bf16: float, peak_kind: str) -> dict:
                 cmp.close()
             except Exception as exc:  # the library has no algorithm for this scaling mode
                 res["cublaslt"] = {"unavailable": str(exc).splitlines()[0][:200]}
+            if kind == "fp8_block128":
+                # cuBLASLt's plain FP8 GEMM (per-tensor scale) on the same bytes:
+                # the library's FP8 tensor throughput, without block scaling.
+                try:
+                    cmp = lowp.CublasLtLowpPlan("fp8_tensor_scaled", a, b, d2, stream=stream)
+                    cmp.run(args.warmup)
+                    t_ms = timed(cmp.run, args.steps)
+                    res["cublaslt_fp8_tensor_scaled"] = {"tflops": flops / (t_ms / 1000.0) / 1e12,
+                                                         "ms_per_step": t_ms,
+                                                         "note": "no block scales: throughput reference only"}
+                    cmp.close()
+                except Exception as exc:
+                    res["cublaslt_fp8_tensor_scaled"] = {"unavailable": str(exc).splitlines()[0][:200]}
             del d2
         out[kind] = res
         del a, b, d

@@ -24,7 +24,8 @@ KINDS = ("nvfp4", "fp8_block128")
 TOL = 2e-2
 FIELDS = ("m", "n", "k", "kind", "cta_group", "tile_m", "tile_n", "grid_ctas", "ours_ms_flushed", "ours_tflops_flushed",
           "ours_tflops_hot", "cublaslt_tflops_flushed", "cublaslt_tflops_hot", "ratio_ours_vs_cublaslt",
-          "cublaslt_note", "rel_frobenius_sampled", "correctness", "gpu_name", "git_commit")
+          "cublaslt_note", "cublaslt_fp8_tensor_scaled_tflops_flushed", "rel_frobenius_sampled", "correctness",
+          "gpu_name", "git_commit")
 
 
 def main(argv=None) -> int:
@@ -102,6 +103,18 @@ def main(argv=None) -> int:
                 ratio = cm.fixed6(cms / ms)
             except Exception as exc:  # no cuBLASLt algorithm for this scaling mode
                 note = str(exc).splitlines()[0][:160].replace(",", ";")
+            fp8_ref = ""
+            if kind == "fp8_block128":
+                # cuBLASLt's plain FP8 GEMM on the same bytes (per-tensor scale,
+                # no block scales): a throughput reference, not the same function.
+                try:
+                    cmp = lowp.CublasLtLowpPlan("fp8_tensor_scaled", a, b, d2, stream=stream)
+                    cmp.run(args.warmup_iterations)
+                    tms, _ = timed(cmp.run)
+                    cmp.close()
+                    fp8_ref = cm.fixed6(flops / tms / 1e9)
+                except Exception:
+                    fp8_ref = ""
             ok = err <= TOL
             failed |= not ok
             rows.append({
@@ -109,7 +122,8 @@ def main(argv=None) -> int:
                 "tile_n": info["tile_n"], "grid_ctas": info["grid_ctas"], "ours_ms_flushed": cm.fixed6(ms),
                 "ours_tflops_flushed": cm.fixed6(flops / ms / 1e9), "ours_tflops_hot": cm.fixed6(flops / hot_ms / 1e9),
                 "cublaslt_tflops_flushed": cl_fl, "cublaslt_tflops_hot": cl_hot, "ratio_ours_vs_cublaslt": ratio,
-                "cublaslt_note": note, "rel_frobenius_sampled": f"{err:.6e}", "correctness": "pass" if ok else "fail",
+                "cublaslt_note": note, "cublaslt_fp8_tensor_scaled_tflops_flushed": fp8_ref,
+                "rel_frobenius_sampled": f"{err:.6e}", "correctness": "pass" if ok else "fail",
                 "gpu_name": gpu.name, "git_commit": commit})
             del a, b, d, d2
         del x, y

@@ -252,7 +252,8 @@ BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k
                                        void* stream, bb_cmp_plan** out, bb_cmp_info* info) {
   try {
     g_err[0] = 0;
-    if (!out || m <= 0 || n <= 0 || k <= 0 || (kind != 1 && kind != 2) || !a || !b || !sfa || !sfb || !d) {
+    if (!out || m <= 0 || n <= 0 || k <= 0 || kind < 1 || kind > 3 || !a || !b || !d ||
+        (kind != 3 && (!sfa || !sfb))) {
       std::snprintf(g_err, sizeof(g_err), "bb_cmp_lowp_plan_create: bad argument");
       return 1;
     }
@@ -265,6 +266,7 @@ BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k
     const cudaDataType_t tab = kind == 1 ? CUDA_R_4F_E2M1 : CUDA_R_8F_E4M3;
     const cublasLtMatmulMatrixScale_t mode =
         kind == 1 ? CUBLASLT_MATMUL_MATRIX_SCALE_VEC16_UE4M3 : CUBLASLT_MATMUL_MATRIX_SCALE_BLK128x128_32F;
+    const bool block_scaled = kind != 3;  // kind 3: plain FP8, no scale tensors
     LT(cublasLtCreate(&p->handle));
     LT(cublasLtMatmulDescCreate(&p->op, CUBLAS_COMPUTE_32F, CUDA_R_32F));
     // Column-major view (the only one the narrow types allow, "TN"):
@@ -278,10 +280,12 @@ BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k
     LT(cublasLtMatrixLayoutCreate(&p->ld, CUDA_R_16BF, n, m, n));
     LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA)));
     LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB)));
-    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_MODE, &mode, sizeof(mode)));
-    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_MODE, &mode, sizeof(mode)));
-    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_POINTER, &sfb, sizeof(sfb)));
-    LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_POINTER, &sfa, sizeof(sfa)));
+    if (block_scaled) {
+      LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_MODE, &mode, sizeof(mode)));
+      LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_MODE, &mode, sizeof(mode)));
+      LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_A_SCALE_POINTER, &sfb, sizeof(sfb)));
+      LT(cublasLtMatmulDescSetAttribute(p->op, CUBLASLT_MATMUL_DESC_B_SCALE_POINTER, &sfa, sizeof(sfa)));
+    }
     cublasLtMatmulPreference_t pref = nullptr;
     LT(cublasLtMatmulPreferenceCreate(&pref));
     size_t ws = kWorkspaceLimit;

@@ -247,9 +247,14 @@ class CublasLtLowpPlan:
     handed over: True passes them as stored ([row block][K block]), False
     passes the transpose ([K block][row block])."""
 
+    CMP_KINDS = {**KINDS, "fp8_tensor_scaled": 3}
+
     def __init__(self, kind: str, a, b, d: torch.Tensor, autotune: bool = False,
                  stream: torch.cuda.Stream | None = None, fp8_scales_kmajor: bool = False):
-        if kind not in KINDS:
+        """kind "fp8_tensor_scaled" runs cuBLASLt's plain FP8 GEMM on the
+        same E4M3 bytes without block scales: a throughput reference for the
+        FP8 block-scaled kernel, not the same function."""
+        if kind not in self.CMP_KINDS:
             raise ValueError(f"unknown kind {kind!r}")
         self._lib = nat.cmp_lib()
         self.stream = stream if stream is not None else torch.cuda.current_stream(d.device)
@@ -258,12 +263,12 @@ class CublasLtLowpPlan:
             sfa, sfb, gscale = a.atoms, b.atoms, a.tensor_scale * b.tensor_scale
         else:
             sfa, sfb, gscale = a.scales, b.scales, 1.0
-            if not fp8_scales_kmajor:
+            if kind != "fp8_tensor_scaled" and not fp8_scales_kmajor:
                 sfa, sfb = sfa.t().contiguous(), sfb.t().contiguous()
         self._keep = (a, b, sfa, sfb, d)
         handle = ctypes.c_void_p()
         info = nat.CmpInfo()
-        rc = self._lib.bb_cmp_lowp_plan_create(KINDS[kind], m, n, k, a.data.data_ptr(), b.data.data_ptr(),
+        rc = self._lib.bb_cmp_lowp_plan_create(self.CMP_KINDS[kind], m, n, k, a.data.data_ptr(), b.data.data_ptr(),
                                                sfa.data_ptr(), sfb.data_ptr(), float(gscale), d.data_ptr(),
                                                1 if autotune else 0, self.stream.cuda_stream, ctypes.byref(handle),
                                                ctypes.byref(info))

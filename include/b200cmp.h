@@ -63,8 +63,10 @@ BB_CMP_API int bb_cmp_plan_create(int64_t m, int64_t n, int64_t k, const void* a
 /* Block-scaled comparator for libb200bench.so's bb_lowp_* GEMM, same
  * operands and D: kind 1 NVFP4 (E2M1 data, VEC16_UE4M3 scales in the
  * 512-byte atom layout, alpha = global_scale), kind 2 FP8 E4M3 with
- * BLK128x128_32F scales. Returns 5 (unsupported) when this cuBLASLt offers
- * no algorithm for the combination. */
+ * BLK128x128_32F scales, kind 3 plain FP8 E4M3 (no scale tensors, sfa /
+ * sfb ignored: a throughput reference for kind 2, not the same function).
+ * Returns 5 (unsupported) when this cuBLASLt offers no algorithm for the
+ * combination. */
 BB_CMP_API int bb_cmp_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const void* a, const void* b,
                                        const void* sfa, const void* sfb, float global_scale, void* d, int autotune,
                                        void* stream, bb_cmp_plan** plan, bb_cmp_info* info);
