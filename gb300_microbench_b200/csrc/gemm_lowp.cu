@@ -56,7 +56,7 @@ constexpr int BM = 128;         // accumulator rows per CTA
 constexpr int ROW_BYTES = 128;  // K bytes of one stage row (one 128-byte swizzle row)
 constexpr int SF_ATOM = 512;    // bytes of one scale atom (128 rows x 4 scales)
 constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr int kLaunchRegs = 168;  // registers per thread the kernels are built for
 constexpr int TMEM_COLS = 512;
 constexpr int BAR_BYTES = 256;
 // Grouped raster: group_m tile-rows are swept across all tile-columns. The
@@ -71,6 +71,17 @@ constexpr int SMEM_LIMIT = 232448;
 // of B scale atoms (each CTA's TMEM needs the scales of every B row).
 template <int kKind, int kCG>
 struct Cfg {
+  // Warp roles: 0 producer, 1 MMA, [EPI_W0, EPI_W0 + 8) epilogue. FP8 runs
+  // a whole control warpgroup (warps 0-3, 2-3 idle) so setmaxnreg can move
+  // registers from it to the two epilogue warpgroups (its promotion keeps a
+  // 128-float accumulator per thread and issues two TMEM loads per wait).
+  static constexpr bool kRegSplit = kKind == kFp8Block;
+  static constexpr int EPI_W0 = kRegSplit ? 4 : 2;
+  static constexpr int THREADS = 32 * EPI_W0 + 32 * EPI_WARPS;
+  static constexpr int CTRL_REGS = 56;   // warpgroup 0 after setmaxnreg.dec
+  static constexpr int EPI_REGS = 224;   // epilogue warpgroups after setmaxnreg.inc
+  static_assert(!kRegSplit || 128 * CTRL_REGS + 256 * EPI_REGS <= THREADS * kLaunchRegs,
+                "register split exceeds the registers the block is launched with");
   static constexpr int TILE_M = BM * kCG;
   static constexpr int TILE_N = 256;
   static constexpr int B_ROWS = TILE_N / kCG;                      // B rows staged per CTA
@@ -250,7 +261,7 @@ __device__ __forceinline__ void promote32(float* acc, const uint32_t (&v)[32], f
 }
 
 template <int kKind, int kCG>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
     bb_lowp_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
                         const __grid_constant__ CUtensorMap tm_d, const Params p) {
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr int STAGES = C::STAGES;
   constexpr bool kPair = kCG == 2;
   const uint32_t rank = kPair ? cluster_ctarank() : 0u;
-  if (blockDim.x != THREADS || (kPair && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
+  if (blockDim.x != C::THREADS || (kPair && cluster_nctarank() != 2) || (gridDim.x % kCG) != 0) {
     if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kDevBadLaunch);
     return;
   }
@@ -315,6 +326,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const int cluster_idx = blockIdx.x / kCG;
 
+  if (warp < C::EPI_W0) {
+    if constexpr (C::kRegSplit) {
+      // Warpgroup 0 (producer, MMA, two idle warps) gives registers to the
+      // epilogue warpgroups (setmaxnreg sits inside each role's branch so
+      // the register allocator sees one limit per region). The host checks
+      // the block's launch register pool covers the split before launching.
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::CTRL_REGS));
+    }
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // The whole warp runs the loop and waits; one elected lane issues.
@@ -470,10 +489,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       bb_wait_warp(smem_u32(mma_done), 0, p.status, kDevTimeoutMma, /*honor_abort=*/false);
     }
+  }
   } else {
+    if constexpr (C::kRegSplit) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::EPI_REGS));
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int half = (warp - 2) / 4;
+    const int half = (warp - C::EPI_W0) / 4;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     uint32_t acc_iter = 0;
     bool ok = true;
@@ -485,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) {
         const uint32_t eb = smem_u32(bar);
         if constexpr (kPair) {
-          mbar_arrive_cluster(mapa_shared(eb, 0));
+          mbar_arrive_cluster_relaxed(mapa_shared(eb, 0));
         } else {
           mbar_arrive(eb);
         }
@@ -496,7 +517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // 32 x 64 boxes: each staged with the 128-byte swizzle in this warp's
     // boxes of shared memory and written by one TMA store (clipped at the
     // edges of D; boxes wholly outside D are skipped).
-    const uint32_t ebuf = smem_u32(smem_epi + (warp - 2) * C::EPI_BOXES * C::EPI_BOX_BYTES);
+    const uint32_t ebuf = smem_u32(smem_epi + (warp - C::EPI_W0) * C::EPI_BOXES * C::EPI_BOX_BYTES);
     uint32_t box_seq = 0;
     const uint64_t d_policy = l2_policy_evict_first();
     auto store_boxes = [&](int row0, int col0_, const uint32_t(&pk_)[64]) {
@@ -584,12 +605,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           const uint32_t taddr = tmem_base + lane_off + buf * 256u + half * 128;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r0[32];
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t r0[32], r1[32];
             tmem_ld_32x32b_x32(taddr + 32 * c, r0);
+            tmem_ld_32x32b_x32(taddr + 32 * (c + 1), r1);
             tmem_ld_wait();
-            if (c == 3) release(buf);
+            if (c == 2) release(buf);
             promote32(acc + 32 * c, r0, s);
+            promote32(acc + 32 * (c + 1), r1, s);
           }
           ++acc_iter;
         }
@@ -639,7 +662,7 @@ template <int kKind, int kCG>
 cudaLaunchConfig_t launch_config(const bb_lowp_plan& pl, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(Cfg<kKind, kCG>::THREADS);
   cfg.dynamicSmemBytes = Cfg<kKind, kCG>::SMEM_BYTES;
   cfg.stream = pl.stream;
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -655,6 +678,17 @@ template <int kKind, int kCG>
 int set_attributes() {
   static bool done = false;  // one attribute call per kernel and process
   if (!done) {
+    if constexpr (Cfg<kKind, kCG>::kRegSplit) {
+      // setmaxnreg.inc waits until the block's register pool can serve it;
+      // refuse to launch a build whose pool is smaller than the split needs.
+      cudaFuncAttributes fa{};
+      BB_CUDA_TRY(cudaFuncGetAttributes(&fa, bb_lowp_gemm_kernel<kKind, kCG>));
+      if (fa.numRegs * Cfg<kKind, kCG>::THREADS < 128 * Cfg<kKind, kCG>::CTRL_REGS + 256 * Cfg<kKind, kCG>::EPI_REGS) {
+        set_error("bb_lowp: kernel built with %d registers per thread; its register split needs %d", fa.numRegs,
+                  kLaunchRegs);
+        return BB_ERR_INTERNAL;
+      }
+    }
     BB_CUDA_TRY(cudaFuncSetAttribute(bb_lowp_gemm_kernel<kKind, kCG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Cfg<kKind, kCG>::SMEM_BYTES));
     done = true;
@@ -785,10 +819,10 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     h->k = k;
     h->stream = static_cast<cudaStream_t>(stream);
     // NVFP4: CTA pairs (256-row tiles) unless A has a single 128-row block.
-    // FP8: single CTAs. Its epilogue promotes every 128-wide K block; the
-    // MMA -> epilogue -> MMA hand-off of the two TMEM partial buffers already
-    // limits one CTA, and across a pair (peer arrivals through the cluster)
-    // it costs far more than the halved B traffic saves.
+    // FP8: single CTAs. Its epilogue promotes every 128-wide K block; that
+    // per-block chain (wait, TMEM loads, release, promotion) bounds both tile
+    // shapes alike (8192^3: 2160 single, 2210 pair TFLOP/s), and the single
+    // CTA has no cross-CTA hand-off.
     // BB_LOWP_CTA_GROUP=1|2 forces one.
     h->cg = (kind == BB_LOWP_NVFP4 && m > 128) ? 2 : 1;
     if (const char* env = std::getenv("BB_LOWP_CTA_GROUP")) {
@@ -873,7 +907,7 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
       info->num_tiles = p.num_tiles;
       info->smem_bytes = h->smem_bytes;
       info->tmem_columns = TMEM_COLS;
-      info->threads_per_cta = THREADS;
+      info->threads_per_cta = kind == BB_LOWP_NVFP4 ? Cfg<kNvfp4, 1>::THREADS : Cfg<kFp8Block, 1>::THREADS;
       info->cta_group = h->cg;
       for (int i = 0; i < 5; ++i) info->reserved[i] = 0;
     }
