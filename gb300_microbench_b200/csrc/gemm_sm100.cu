@@ -468,7 +468,9 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
       if (lane == 0) {
         const uint32_t eb = smem_u32(&tmem_empty[acc]);
         if constexpr (kCG == 2) {
-          mbar_arrive_cluster(mapa_shared(eb, 0));
+          // Relaxed: the TMEM reads this publishes completed at
+          // tcgen05.wait::ld; a cluster-scope release arrive is far slower.
+          mbar_arrive_cluster_relaxed(mapa_shared(eb, 0));
         } else {
           mbar_arrive(eb);
         }
