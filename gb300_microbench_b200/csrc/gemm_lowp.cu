@@ -75,7 +75,15 @@ struct Cfg {
   // a whole control warpgroup (warps 0-3, 2-3 idle) so setmaxnreg can move
   // registers from it to the two epilogue warpgroups (its promotion keeps a
   // 128-float accumulator per thread and issues two TMEM loads per wait).
-  static constexpr bool kRegSplit = kKind == kFp8Block;
+  // Tiles are 256 columns wide. The code also supports 128-wide FP8 tiles
+  // (four 128-column TMEM partial buffers, 64 accumulators per epilogue
+  // thread): as CTA pairs they measured 1.25 PFLOP/s at 8192^3 against 2.2
+  // for 256-wide tiles, the MMA warp's two barrier waits per 128-K block
+  // then costing as much as the block's 256 clocks of MMA work.
+  static constexpr int TILE_N = 256;
+  static constexpr int WARP_COLS = TILE_N / 2;         // epilogue columns per warp
+  static constexpr int FP8_BUFS = TMEM_COLS / TILE_N;  // FP8 partial buffers
+  static constexpr bool kRegSplit = kKind == kFp8Block && WARP_COLS == 128;
   static constexpr int EPI_W0 = kRegSplit ? 4 : 2;
   static constexpr int THREADS = 32 * EPI_W0 + 32 * EPI_WARPS;
   static constexpr int CTRL_REGS = 56;   // warpgroup 0 after setmaxnreg.dec
@@ -83,7 +91,6 @@ struct Cfg {
   static_assert(!kRegSplit || 128 * CTRL_REGS + 256 * EPI_REGS <= THREADS * kLaunchRegs,
                 "register split exceeds the registers the block is launched with");
   static constexpr int TILE_M = BM * kCG;
-  static constexpr int TILE_N = 256;
   static constexpr int B_ROWS = TILE_N / kCG;                      // B rows staged per CTA
   static constexpr int K_PER_STAGE = kKind == kNvfp4 ? 256 : 128;  // elements
   static constexpr int MMA_K = kKind == kNvfp4 ? 64 : 32;          // elements per instruction
@@ -106,7 +113,7 @@ struct Cfg {
   static constexpr int STAGES = STAGES_FIT < STAGES_MAX ? STAGES_FIT : STAGES_MAX;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(STAGES >= 3, "ring too shallow");
-  static_assert((2 * STAGES + 8) * 8 <= BAR_BYTES, "barrier area");
+  static_assert((2 * STAGES + 12) * 8 <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
   static_assert(MMAS * 32 == ROW_BYTES, "one instruction consumes 32 bytes of each row");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
@@ -283,11 +290,11 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + C::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* acc_full = bars + 2 * STAGES;       // [2]
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2], in the leader CTA: buffer fully drained
-  uint64_t* ovl_free = bars + 2 * STAGES + 4;   // [2], in the leader CTA: NVFP4 shared subtile drained
-  uint64_t* mma_done = bars + 2 * STAGES + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
+  uint64_t* acc_full = bars + 2 * STAGES;       // [4]
+  uint64_t* acc_empty = bars + 2 * STAGES + 4;  // [4], in the leader CTA: buffer fully drained
+  uint64_t* ovl_free = bars + 2 * STAGES + 8;   // [2], in the leader CTA: NVFP4 shared subtile drained
+  uint64_t* mma_done = bars + 2 * STAGES + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 11);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -307,11 +314,11 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 4; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), EPI_WARPS * kCG);
-      mbar_init(smem_u32(&ovl_free[b]), (EPI_WARPS / 2) * kCG);
     }
+    for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&ovl_free[b]), (EPI_WARPS / 2) * kCG);
     mbar_init(smem_u32(mma_done), 1);
     fence_mbarrier_init_cluster();
   }
@@ -429,14 +436,14 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
           uint32_t d_tmem = tmem_base + acc_col;
           uint32_t buf = 0;
           if constexpr (kKind == kFp8Block) {
-            buf = acc_iter & 1u;
-            if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[buf]), ((acc_iter >> 1) & 1u) ^ 1u, p.status,
+            buf = acc_iter % C::FP8_BUFS;
+            if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[buf]), ((acc_iter / C::FP8_BUFS) & 1u) ^ 1u, p.status,
                                      kDevTimeoutMma)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            d_tmem = tmem_base + buf * 256u;
+            d_tmem = tmem_base + buf * C::TILE_N;
           }
           if (!bb_wait_warp<kPair>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
             ok = false;
@@ -520,9 +527,9 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
     const uint32_t ebuf = smem_u32(smem_epi + (warp - C::EPI_W0) * C::EPI_BOXES * C::EPI_BOX_BYTES);
     uint32_t box_seq = 0;
     const uint64_t d_policy = l2_policy_evict_first();
-    auto store_boxes = [&](int row0, int col0_, const uint32_t(&pk_)[64]) {
+    auto store_boxes = [&](int row0, int col0_, const uint32_t(&pk_)[C::WARP_COLS / 2]) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < C::WARP_COLS / 64; ++h) {
         const uint32_t buf = ebuf + (box_seq % C::EPI_BOXES) * C::EPI_BOX_BYTES;
         ++box_seq;
         if (lane == 0) bulk_wait_group_read<C::EPI_BOXES - 1>();
@@ -545,13 +552,13 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
       int m_blk, n_blk;
       tile_coords(p, t, m_blk, n_blk);
       const int row = m_blk * C::TILE_M + static_cast<int>(rank) * BM + q * 32 + lane;
-      const int col0 = n_blk * C::TILE_N + half * 128;
-      uint32_t pk[64];
+      const int col0 = n_blk * C::TILE_N + half * C::WARP_COLS;
+      uint32_t pk[C::WARP_COLS / 2];
       if constexpr (kKind == kNvfp4) {
         const uint32_t b = acc_iter & 1u;
         if (!bb_wait_warp<kPair>(smem_u32(&acc_full[b]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) break;
         tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_off + b * kAccStride + half * 128;
+        const uint32_t taddr = tmem_base + lane_off + b * kAccStride + half * C::WARP_COLS;
         // The subtile shared with the other buffer is columns [192, 256) of
         // buffer 0 (this warp's chunks 2, 3 when half == 1) and [0, 64) of
         // buffer 1 (chunks 0, 1 when half == 0); its owners read it first
@@ -584,33 +591,34 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
         // Ragged edges: rows / columns past M / N are never stored, any valid
         // scale row serves them.
         const int mb = min(m_blk * kCG + static_cast<int>(rank), p.rb_m - 1);
-        const int nb = min(2 * n_blk + half, p.rb_n - 1);
+        const int nb = min(col0 / 128, p.rb_n - 1);
         const float* sa_row = sa + static_cast<int64_t>(mb) * p.k_stages;
         const float* sb_row = sb + static_cast<int64_t>(nb) * p.k_stages;
-        float acc[128];
+        float acc[C::WARP_COLS];
 #pragma unroll
-        for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+        for (int j = 0; j < C::WARP_COLS; ++j) acc[j] = 0.f;
         float s_next = __ldg(sa_row) * __ldg(sb_row);
         for (int ks = 0; ks < p.k_stages; ++ks) {
           const float s = s_next;
           if (ks + 1 < p.k_stages) s_next = __ldg(sa_row + ks + 1) * __ldg(sb_row + ks + 1);
-          const uint32_t buf = acc_iter & 1u;
+          const uint32_t buf = acc_iter % C::FP8_BUFS;
           // Spin without the suspend hint: this wait is on the per-K-block
           // MMA -> promotion -> MMA hand-off, where wake-up latency counts.
-          if (!bb_wait_warp<kPair, false>(smem_u32(&acc_full[buf]), (acc_iter >> 1) & 1u, p.status,
+          if (!bb_wait_warp<kPair, false>(smem_u32(&acc_full[buf]), (acc_iter / C::FP8_BUFS) & 1u, p.status,
                                           kDevTimeoutEpilogue)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t taddr = tmem_base + lane_off + buf * 256u + half * 128;
+          const uint32_t taddr = tmem_base + lane_off + buf * C::TILE_N + half * C::WARP_COLS;
+          constexpr int kChunks = C::WARP_COLS / 32;
 #pragma unroll
-          for (int c = 0; c < 4; c += 2) {
+          for (int c = 0; c < kChunks; c += 2) {
             uint32_t r0[32], r1[32];
             tmem_ld_32x32b_x32(taddr + 32 * c, r0);
             tmem_ld_32x32b_x32(taddr + 32 * (c + 1), r1);
             tmem_ld_wait();
-            if (c == 2) release(buf);
+            if (c == kChunks - 2) release(buf);
             promote32(acc + 32 * c, r0, s);
             promote32(acc + 32 * (c + 1), r1, s);
           }
@@ -618,7 +626,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
         }
         if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) pack32(acc + 32 * c, p.global_scale, pk + 16 * c);
+        for (int c = 0; c < C::WARP_COLS / 32; ++c) pack32(acc + 32 * c, p.global_scale, pk + 16 * c);
       }
       store_boxes(row - lane, col0, pk);
     }
@@ -642,6 +650,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
 struct bb_lowp_plan {
   int kind = 0;
   int cg = 1;
+  int tile_n = 256;
   int stages = 0;
   int64_t m = 0, n = 0, k = 0;
   cudaStream_t stream = nullptr;
@@ -736,6 +745,7 @@ template <int kKind, int kCG>
 void plan_geometry(bb_lowp_plan& h, int sm_count) {
   using C = Cfg<kKind, kCG>;
   h.stages = C::STAGES;
+  h.tile_n = C::TILE_N;
   h.smem_bytes = C::SMEM_BYTES;
   Params& p = h.params;
   p.tiles_m = static_cast<int32_t>((h.m + C::TILE_M - 1) / C::TILE_M);
@@ -847,7 +857,7 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     if (rc == BB_OK) {
       const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(n)};
       const uint64_t strides[1] = {row_bytes};
-      const uint32_t box[2] = {ROW_BYTES, static_cast<uint32_t>(256 / h->cg)};
+      const uint32_t box[2] = {ROW_BYTES, static_cast<uint32_t>(h->tile_n / h->cg)};
       rc = encode_tiled(&h->tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 2, b, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     }
@@ -900,7 +910,7 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     if (info) {
       info->kind = kind;
       info->tile_m = 128 * h->cg;
-      info->tile_n = 256;
+      info->tile_n = h->tile_n;
       info->tile_k = k_step;
       info->stages = h->stages;
       info->grid_ctas = h->grid;
