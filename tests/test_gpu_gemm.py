@@ -142,6 +142,20 @@ def test_run_host_pipelined(cuda_device, mnk, dtype):
     plan.close()
 
 
+def test_run_host_batched_serial_path(cuda_device):
+    """Batched problems (L > 1) take the serial host path."""
+    a, b = inputs.reference_mode_operands(512, 264, 128, l=2)
+    ad = torch.empty_like(a, device=cuda_device)
+    bd = torch.empty_like(b, device=cuda_device)
+    c = torch.empty(2, 512, 264, dtype=torch.float32, device=cuda_device)
+    plan = GemmPlan(ad, bd, c)
+    c_host = torch.full((2, 512, 264), float("nan"), dtype=torch.float32).pin_memory()
+    plan.run_host(a.contiguous().pin_memory(), b.contiguous().pin_memory(), c_host)
+    for i in range(2):
+        assert torch.equal(c_host[i], oracle.gemm_reference_fp32(a[i], b[i]))
+    plan.close()
+
+
 def test_cublaslt_comparator_agrees(cuda_device):
     a, b = inputs.baseline_mode_operands(1024, 1024, 1024)
     ad, bd = a.to(cuda_device), b.to(cuda_device)
