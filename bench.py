@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
-"""Headline benchmark: the sm_100a BF16 GEMM on BASELINE config 0.
+"""Headline benchmark: the sm_100a BF16 GEMM on config 0 (4096^3 per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
 
-Workload: C = A * B^T with A (M x K) and B (N x K)
+Workload (config 0): C = A * B^T with A (M x K) and B (N x K)
 BF16 from N(0,1) (torch.Generator seed 0), FP32 accumulation, BF16 C, M = N =
 K = 4096 per GPU. At N GPUs the global problem is (4096 N) x 4096 x 4096 with
 A and C row-sharded (rank r owns rows [4096 r, 4096 (r+1))) and B replicated:
@@ -45,7 +45,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 
 def parse_args(argv=None):
-    ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on BASELINE config 0 (4096^3 per GPU)")
+    ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on config 0 (4096^3 per GPU)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -253,7 +253,7 @@ def run_reference(args, world, rank):
     return 0
 
 
-LOWP_DIM = 8192  # (M, N, K) = (8192, 8192, 8192)
+LOWP_DIM = 8192  # block-scaled GEMMs (config 4): (M, N, K) = (8192, 8192, 8192)
 # Dense tensor rate per clock relative to BF16, measured with the UMMA probe
 # on this pool's B200s (kind::f16 8191, kind::f8f6f4 16381, kind::mxf4nvf4
 # 32762 FLOP/clk/SM for 128 x 256 instructions).
@@ -261,7 +261,7 @@ LOWP_RATE_VS_BF16 = {"fp8_block128": 2.0, "nvfp4": 4.0}
 
 
 def run_lowp(args, stream, flush, peak_bf16: float, peak_kind: str) -> dict:
-    """Block-scaled GEMMs of BASELINE config 4 at 8192^3 on this GPU: the
+    """Block-scaled GEMMs (config 4) at 8192^3 on this GPU: the
     FP8 (128 x 128 FP32 block scales) and NVFP4 (UE4M3 per 16 + FP32 tensor
     scale) kernels, L2 flushed before every step, checked on sampled rows
     against the FP32 product of the dequantised inputs."""

@@ -20,7 +20,7 @@ reference's candidate (tile, cluster, 2-CTA instructions, scheduler), and the
 provenance columns carry this build's identities in the same formats.
 
 Baseline mode (``--mode baseline``) measures the same shapes in the
-BASELINE.json contract: N(0,1) operands from ``torch.Generator`` seed 0,
+baseline contract: N(0,1) operands from ``torch.Generator`` seed 0,
 BF16 C, relative Frobenius error <= 1e-2, and adds the ``tuned`` candidate;
 its CSV carries ``schema_version=b200.baseline.v1`` and five candidates per
 shape.

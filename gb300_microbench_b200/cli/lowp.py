@@ -1,4 +1,4 @@
-"""Block-scaled GEMM sweep: FP8 E4M3 with 128 x 128 FP32
+"""Block-scaled GEMM sweep (8192^3 and three more shapes): FP8 E4M3 with 128 x 128 FP32
 block scales and NVFP4 (E2M1, UE4M3 per 16 K, FP32 per tensor), BF16 D, on
 one GPU, with cuBLASLt's block-scaled GEMM on the same operands beside it.
 

@@ -1,5 +1,5 @@
 """Multi-GPU GEMM sweep: the five frozen shapes (gemm_comparison.py:116-122)
-row-sharded over the ranks of one node, B replicated, in BASELINE mode
+row-sharded over the ranks of one node, B replicated, in baseline mode
 (N(0,1) seed-0 BF16 operands, BF16 C). One process per GPU:
 
     python -m torch.distributed.run --nproc-per-node P --master-addr 127.0.0.1 \\

@@ -8,7 +8,7 @@ sm_100a probes of libb200bench.so.
         --repetitions N [--operands {pattern,random}] [--seed N]
 
 Flags, exit codes and the 37-column CSV are the reference's
-(umma_1sm.cu:965-995); depths 32 and 128 (the BASELINE grid) and N(0,1)
+(umma_1sm.cu:965-995); depths 32 and 128 (the baseline-mode grid) and N(0,1)
 operands (``--operands random``, checked against an FP32 host
 restatement of depth * A * B^T within 1e-5 relative Frobenius error) are
 additions. Pattern operands are checked for exact equality, every

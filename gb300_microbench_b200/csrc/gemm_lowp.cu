@@ -1,4 +1,4 @@
-// Block-scaled low-precision GEMMs for sm_100a:
+// Block-scaled low-precision GEMMs for sm_100a (FP8 128 x 128-block, NVFP4):
 //   D (M x N, BF16) = dequant(A) (M x K) * dequant(B)^T (N x K), FP32 accumulate.
 //
 // Two operand formats, one persistent warp-specialised kernel:

@@ -6,7 +6,7 @@
 // non-swizzled K-major core-matrix layout (8 rows x 16 bytes per core
 // matrix; the two 8-element K halves LBO = 128 B apart, successive 8-row
 // groups SBO = 256 B apart), so the same kernel serves the reference's
-// integer patterns and the BASELINE N(0,1) operands. One elected thread of
+// integer patterns and the baseline-mode N(0,1) operands. One elected thread of
 // CTA rank 0 issues DEPTH dependent MMAs per iteration (the first with
 // enable_input_d = 0), commits to its own mbarrier and waits for it (bounded)
 // before the next iteration; %clock64 brackets the loop.

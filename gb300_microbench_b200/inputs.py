@@ -8,7 +8,7 @@ tensor of shape (L, rows, K) filled by ``random_(-2, 2)`` (values -2..1),
 converted to float and then to BF16, A first, then B. :func:`reference_mode_operands`
 restates that draw without the helper.
 
-BASELINE mode: A (M, K) then B (N, K) from N(0, 1) with
+Baseline mode: A (M, K) then B (N, K) from N(0, 1) with
 ``torch.Generator().manual_seed(0)`` on the CPU, cast to BF16.
 """
 from __future__ import annotations
@@ -49,7 +49,7 @@ def umma_pattern_operands(cta_group: int, n: int) -> tuple[torch.Tensor, torch.T
 
 
 def umma_random_operands(cta_group: int, n: int, seed: int = BASELINE_SEED) -> tuple[torch.Tensor, torch.Tensor]:
-    """BASELINE-mode UMMA operands: N(0, 1) BF16 from a seeded generator."""
+    """Baseline-mode UMMA operands: N(0, 1) BF16 from a seeded generator."""
     g = torch.Generator().manual_seed(seed)
     a = torch.randn(128 * cta_group, 16, generator=g).to(torch.bfloat16)
     b = torch.randn(n, 16, generator=g).to(torch.bfloat16)

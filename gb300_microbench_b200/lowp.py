@@ -1,4 +1,4 @@
-"""Low-precision operand formats of the block-scaled GEMMs.
+"""Low-precision operand formats of the block-scaled GEMMs (8192^3 FP8 128 x 128-block and NVFP4).
 
 NVFP4: E2M1 values (two per byte, element 2i in the low nibble), one
 UE4M3 scale per 16 consecutive K elements, and one FP32 scale per tensor:
@@ -168,7 +168,7 @@ class Fp8BlockOperand:
 
 
 def config4_inputs(m: int, n: int, k: int, seed: int = 0, device: str | torch.device = "cuda"):
-    """The FP32 inputs of BASELINE config 4: A (M, K) and B (N, K) ~ N(0, 1)
+    """The FP32 inputs of the block-scaled GEMMs: A (M, K) and B (N, K) ~ N(0, 1)
     from torch.Generator(seed) (the generator config 0 uses)."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     a = torch.randn(m, k, generator=g)

@@ -5,7 +5,7 @@ rank runs the single-GPU kernel on its (rows, N, K) block, so the timed
 path has no collective. ``gather_rows`` reassembles C on every rank with one
 all-gather for validation only (NCCL on GPUs, gloo in the CPU tests).
 
-This is the multi-GPU mode the BASELINE contract adds to the reference,
+This is the multi-GPU mode this build adds to the reference,
 which is strictly single-GPU (memory_paths/ldgsts.cu:396-398,
 gemm_comparison.py:1098-1108).
 """

@@ -1,6 +1,6 @@
 """CPU oracle for the block-scaled GEMMs. TEST INFRASTRUCTURE ONLY.
 
-The reference has no low-precision GEMM (BASELINE config 4 is new work), so
+The reference has no low-precision GEMM (this path is new work), so
 this module restates the operand formats from their published definitions
 and the check the configuration names: an FP32 matmul of the dequantised
 inputs, relative Frobenius error <= 2e-2.
@@ -79,5 +79,5 @@ def fp8_block_dequant(q: np.ndarray, scales: np.ndarray, block: int = 128) -> np
 
 
 def gemm_dequant_fp32(a_deq: np.ndarray, b_deq: np.ndarray) -> np.ndarray:
-    """The check of BASELINE config 4: FP32 matmul of the dequantised inputs."""
+    """The block-scaled GEMMs' check: FP32 matmul of the dequantised inputs."""
     return a_deq.astype(np.float32) @ b_deq.astype(np.float32).T

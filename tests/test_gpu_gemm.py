@@ -2,7 +2,7 @@
 
 Reference mode (integer operands, FP32 C) must be exact; the reference's
 elementwise check (|d| <= 0.1 + 1e-5 |ref|, gemm_comparison.py:2718-2755) is
-applied as well. BASELINE mode (N(0,1) operands, BF16 C) must be within a
+applied as well. Baseline mode (N(0,1) operands, BF16 C) must be within a
 relative Frobenius error of 1e-2 of the FP32 oracle.
 """
 import pytest
@@ -14,7 +14,7 @@ from gb300_microbench_b200.gemm import VARIANTS, CublasLtPlan, GemmPlan
 
 pytestmark = pytest.mark.gpu
 
-BF16_TOL = 1e-2  # relative Frobenius
+BF16_TOL = 1e-2  # relative Frobenius bound of baseline mode (N(0,1) operands, BF16 C)
 
 
 def _run(a, b, out_dtype, variant, dev):

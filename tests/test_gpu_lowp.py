@@ -1,4 +1,4 @@
-"""Block-scaled GEMM parity on the GPU through the C ABI.
+"""Block-scaled GEMM parity on the GPU (FP8 128 x 128-block, NVFP4) through the C ABI.
 
 Two kinds of cases per format:
 * exact: operands encoded directly with power-of-two block scales and small
@@ -19,7 +19,7 @@ from gb300_microbench_b200 import lowp
 
 pytestmark = pytest.mark.gpu
 
-LOWP_TOL = 2e-2  # relative Frobenius
+LOWP_TOL = 2e-2  # relative Frobenius bound of the block-scaled GEMMs
 
 
 def _e4m3_pow2(exps: torch.Tensor) -> torch.Tensor:

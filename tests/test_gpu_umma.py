@@ -1,5 +1,5 @@
 """UMMA probes on the GPU: exact known answers (reference mode) and
-N(0,1) operands against the double-precision oracle (BASELINE mode)."""
+N(0,1) operands against the double-precision oracle (baseline mode)."""
 import numpy as np
 import pytest
 import torch
