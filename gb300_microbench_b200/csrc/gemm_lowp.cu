@@ -101,9 +101,10 @@ struct Cfg {
   static constexpr int SFB_BYTES = kKind == kNvfp4 ? 2 * MMAS * SF_ATOM : 0;  // two row blocks
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   // Epilogue staging: per epilogue warp EPI_BOXES boxes of 32 rows x 128
-  // bytes (64 BF16 columns), written to D by TMA stores. Two per warp for
-  // the CTA pair (its ring is smaller), one otherwise.
-  static constexpr int EPI_BOXES = kCG == 2 ? 2 : 1;
+  // bytes (64 BF16 columns), written to D by TMA stores. One box per warp:
+  // a second one cost the NVFP4 pair its fifth ring stage (6170 -> 6512
+  // TFLOP/s at 8192^3 with one box and five stages).
+  static constexpr int EPI_BOXES = 1;
   static constexpr int EPI_BOX_BYTES = 32 * 128;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BOXES * EPI_BOX_BYTES;
   static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
