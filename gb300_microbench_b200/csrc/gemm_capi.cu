@@ -196,6 +196,41 @@ int init_pipe(bb_gemm_plan* plan) {
   return BB_OK;
 }
 
+// Queues the pipelined host-buffer run: B, then A chunk by chunk on the
+// H2D stream; each chunk's GEMM on the plan's stream after its rows landed;
+// its C rows on the D2H stream after its GEMM.
+int enqueue_pipe(bb_gemm_plan* plan, const void* a_host, const void* b_host, void* c_host, size_t b_bytes,
+                 size_t es) {
+  using namespace bb;
+  gemm::Plan& p = plan->p;
+  HostPipe& hp = plan->pipe;
+  BB_CUDA_TRY(cudaEventRecord(hp.ev_b, p.stream));
+  BB_CUDA_TRY(cudaStreamWaitEvent(hp.h2d, hp.ev_b, 0));
+  BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, hp.h2d));
+  BB_CUDA_TRY(cudaEventRecord(hp.ev_b, hp.h2d));
+  for (int i = 0; i < hp.chunks; ++i) {
+    const size_t off = static_cast<size_t>(hp.row0[i]) * p.k * 2;
+    BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(const_cast<void*>(p.a)) + off,
+                                static_cast<const uint8_t*>(a_host) + off, static_cast<size_t>(hp.rows[i]) * p.k * 2,
+                                cudaMemcpyHostToDevice, hp.h2d));
+    BB_CUDA_TRY(cudaEventRecord(hp.ev_a[i], hp.h2d));
+  }
+  BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_b, 0));
+  for (int i = 0; i < hp.chunks; ++i) {
+    BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_a[i], 0));
+    int rc = hp.sub[i].launch(hp.sub[i]);
+    if (rc != BB_OK) return rc;
+    ++p.launches;
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    BB_CUDA_TRY(cudaEventRecord(hp.ev_c[i], p.stream));
+    BB_CUDA_TRY(cudaStreamWaitEvent(hp.d2h, hp.ev_c[i], 0));
+    const size_t coff = static_cast<size_t>(hp.row0[i]) * p.n * es;
+    BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(c_host) + coff, static_cast<const uint8_t*>(p.c) + coff,
+                                static_cast<size_t>(hp.rows[i]) * p.n * es, cudaMemcpyDeviceToHost, hp.d2h));
+  }
+  return BB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -297,6 +332,10 @@ BB_API int bb_gemm_execute_n(bb_gemm_plan* plan, int iterations) {
       set_error("bb_gemm_execute: null plan");
       return BB_ERR_ARGUMENT;
     }
+    if (iterations < 0) {
+      set_error("bb_gemm_execute: negative iteration count %d", iterations);
+      return BB_ERR_ARGUMENT;
+    }
     for (int i = 0; i < iterations; ++i) {
       int rc = plan->p.launch(plan->p);
       if (rc != BB_OK) return rc;
@@ -354,38 +393,30 @@ BB_API int bb_gemm_run_host(bb_gemm_plan* plan, const void* a_host, const void* 
     if (!hp.ready || p.epi_mode != hp.sub[0].epi_mode || p.alpha != hp.sub[0].alpha || p.beta != hp.sub[0].beta) {
       // Serial path (batched problems, few rows, or an epilogue changed
       // since the pipeline was built).
-      BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.a), a_host, a_bytes, cudaMemcpyHostToDevice, p.stream));
-      BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, p.stream));
-      int rc = bb_gemm_execute_n(plan, 1);
-      if (rc != BB_OK) return rc;
-      BB_CUDA_TRY(cudaMemcpyAsync(c_host, p.c, c_bytes, cudaMemcpyDeviceToHost, p.stream));
+      int rc = check_cuda(cudaMemcpyAsync(const_cast<void*>(p.a), a_host, a_bytes, cudaMemcpyHostToDevice, p.stream),
+                          "cudaMemcpyAsync(A)");
+      if (rc == BB_OK)
+        rc = check_cuda(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, p.stream),
+                        "cudaMemcpyAsync(B)");
+      if (rc == BB_OK) rc = bb_gemm_execute_n(plan, 1);
+      if (rc == BB_OK)
+        rc = check_cuda(cudaMemcpyAsync(c_host, p.c, c_bytes, cudaMemcpyDeviceToHost, p.stream), "cudaMemcpyAsync(C)");
+      if (rc != BB_OK) {
+        cudaStreamSynchronize(p.stream);  // no copy may touch the host buffers after the call
+        return rc;
+      }
       return bb_gemm_synchronize(plan);
     }
     // Pipelined path. Work queued earlier on the plan's stream finishes
-    // before the copies overwrite A and B.
-    BB_CUDA_TRY(cudaEventRecord(hp.ev_b, p.stream));
-    BB_CUDA_TRY(cudaStreamWaitEvent(hp.h2d, hp.ev_b, 0));
-    BB_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(p.b), b_host, b_bytes, cudaMemcpyHostToDevice, hp.h2d));
-    BB_CUDA_TRY(cudaEventRecord(hp.ev_b, hp.h2d));
-    for (int i = 0; i < hp.chunks; ++i) {
-      const size_t off = static_cast<size_t>(hp.row0[i]) * p.k * 2;
-      BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(const_cast<void*>(p.a)) + off,
-                                  static_cast<const uint8_t*>(a_host) + off, static_cast<size_t>(hp.rows[i]) * p.k * 2,
-                                  cudaMemcpyHostToDevice, hp.h2d));
-      BB_CUDA_TRY(cudaEventRecord(hp.ev_a[i], hp.h2d));
-    }
-    BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_b, 0));
-    for (int i = 0; i < hp.chunks; ++i) {
-      BB_CUDA_TRY(cudaStreamWaitEvent(p.stream, hp.ev_a[i], 0));
-      int rc = hp.sub[i].launch(hp.sub[i]);
-      if (rc != BB_OK) return rc;
-      ++p.launches;
-      g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-      BB_CUDA_TRY(cudaEventRecord(hp.ev_c[i], p.stream));
-      BB_CUDA_TRY(cudaStreamWaitEvent(hp.d2h, hp.ev_c[i], 0));
-      const size_t coff = static_cast<size_t>(hp.row0[i]) * p.n * es;
-      BB_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(c_host) + coff, static_cast<const uint8_t*>(p.c) + coff,
-                                  static_cast<size_t>(hp.rows[i]) * p.n * es, cudaMemcpyDeviceToHost, hp.d2h));
+    // before the copies overwrite A and B. If queuing fails part-way, the
+    // copy streams are drained before returning, so no copy still reads or
+    // writes the caller's host buffers after the call.
+    const int rc = enqueue_pipe(plan, a_host, b_host, c_host, b_bytes, es);
+    if (rc != BB_OK) {
+      cudaStreamSynchronize(hp.h2d);
+      cudaStreamSynchronize(hp.d2h);
+      cudaStreamSynchronize(p.stream);
+      return rc;
     }
     BB_CUDA_TRY(cudaStreamSynchronize(hp.d2h));
     return bb_gemm_synchronize(plan);

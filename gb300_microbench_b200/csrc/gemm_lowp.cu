@@ -940,6 +940,10 @@ BB_API int bb_lowp_execute_n(bb_lowp_plan* plan, int iterations) {
       set_error("bb_lowp_execute_n: null plan");
       return BB_ERR_ARGUMENT;
     }
+    if (iterations < 0) {
+      set_error("bb_lowp_execute: negative iteration count %d", iterations);
+      return BB_ERR_ARGUMENT;
+    }
     for (int i = 0; i < iterations; ++i) {
       int rc = launch(*plan);
       if (rc != BB_OK) return rc;

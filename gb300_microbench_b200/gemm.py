@@ -61,10 +61,14 @@ class GemmPlan:
             raise ValueError("C must be bfloat16 or float32")
         if variant not in VARIANTS:
             raise ValueError(f"unknown variant {variant!r}; expected one of {sorted(VARIANTS)}")
+        if not (a.device == b.device == c.device):
+            raise ValueError(f"A, B, C on {a.device}, {b.device}, {c.device}: all must be on one device")
         self.m, self.n, self.k, self.l = _dims(a, b, c)
         self.a, self.b, self.c = a, b, c
         self.variant = variant
         self.stream = stream if stream is not None else torch.cuda.current_stream(a.device)
+        if self.stream.device != a.device:
+            raise ValueError(f"stream on {self.stream.device}, tensors on {a.device}")
         self._lib = nat.bench_lib()
         handle = ctypes.c_void_p()
         info = nat.GemmInfo()
@@ -103,7 +107,7 @@ class GemmPlan:
         if beta != 0.0:
             if c_src is None:
                 raise ValueError("beta != 0 needs c_src")
-            if c_src.shape != self.c.shape or c_src.dtype != self.c.dtype or not c_src.is_contiguous() or not c_src.is_cuda:
+            if c_src.shape != self.c.shape or c_src.dtype != self.c.dtype or not c_src.is_contiguous() or c_src.device != self.c.device:
                 raise ValueError("c_src must be a contiguous CUDA tensor with C's shape and dtype")
             self._c_src = c_src
             ptr = c_src.data_ptr()
@@ -154,12 +158,23 @@ class CublasLtPlan:
 
     def __init__(self, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, autotune: bool = False,
                  stream: torch.cuda.Stream | None = None, layout: str = "column"):
-        if a.dim() != 2:
+        if not (a.dim() == b.dim() == c.dim() == 2):
             raise ValueError("the comparator takes 2-D operands")
-        self._lib = nat.cmp_lib()
-        self.stream = stream if stream is not None else torch.cuda.current_stream(a.device)
+        for name, t in (("A", a), ("B", b), ("C", c)):
+            _check_tensor(name, t)
+        if not (a.device == b.device == c.device):
+            raise ValueError(f"A, B, C on {a.device}, {b.device}, {c.device}: all must be on one device")
+        if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or c.dtype not in _DTYPES:
+            raise ValueError("A and B must be bfloat16, C bfloat16 or float32")
+        if layout not in self.LAYOUTS:
+            raise ValueError(f"unknown layout {layout!r}; expected one of {sorted(self.LAYOUTS)}")
         m, k = a.shape
         n = b.shape[0]
+        if tuple(b.shape) != (n, k) or tuple(c.shape) != (m, n) or b.shape[1] != k:
+            raise ValueError(f"shape mismatch: A{tuple(a.shape)} B{tuple(b.shape)} C{tuple(c.shape)}")
+        self._lib = nat.cmp_lib()
+        self.stream = stream if stream is not None else torch.cuda.current_stream(a.device)
+        self._c = c
         handle = ctypes.c_void_p()
         info = nat.CmpInfo()
         rc = self._lib.bb_cmp_plan_create(m, n, k, a.data_ptr(), b.data_ptr(), c.data_ptr(), _DTYPES[c.dtype],
@@ -175,8 +190,12 @@ class CublasLtPlan:
 
     def set_epilogue(self, alpha: float = 1.0, beta: float = 0.0, c_src: torch.Tensor | None = None) -> None:
         """Later executions compute D = alpha * A @ B^T + beta * c_src."""
-        if beta != 0.0 and c_src is None:
-            raise ValueError("beta != 0 needs c_src")
+        if beta != 0.0:
+            if c_src is None:
+                raise ValueError("beta != 0 needs c_src")
+            if (c_src.shape != self._c.shape or c_src.dtype != self._c.dtype or not c_src.is_contiguous()
+                    or c_src.device != self._c.device):
+                raise ValueError("c_src must be a contiguous CUDA tensor with C's shape and dtype")
         self._c_src = c_src
         rc = self._lib.bb_cmp_plan_set_epilogue(self._handle, float(alpha), float(beta),
                                                 c_src.data_ptr() if beta != 0.0 else None)

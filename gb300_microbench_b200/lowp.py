@@ -180,6 +180,31 @@ def config4_inputs(m: int, n: int, k: int, seed: int = 0, device: str | torch.de
 KINDS = {"nvfp4": nat.BB_LOWP_NVFP4, "fp8_block128": nat.BB_LOWP_FP8_BLOCK128}
 
 
+def _check_buffers(kind: str, a, b, d: torch.Tensor, sfa: torch.Tensor, sfb: torch.Tensor, stream) -> None:
+    """Every buffer on D's device, contiguous, and at least as large as the
+    native side reads: its tensor maps and scale loads are sized from M, N
+    and K, not from the buffers."""
+    if b.k != a.k or tuple(d.shape) != (a.rows, b.rows):
+        raise ValueError("shape mismatch between A, B and D")
+    for t in (a.data, b.data, sfa, sfb):
+        if not t.is_cuda or not t.is_contiguous():
+            raise ValueError("operands must be contiguous CUDA tensors")
+        if t.device != d.device:
+            raise ValueError(f"operands on {t.device}, D on {d.device}: all must be on one device")
+    if stream.device != d.device:
+        raise ValueError(f"stream on {stream.device}, tensors on {d.device}")
+    row_bytes = a.k // 2 if kind == "nvfp4" else a.k
+    for name, op in (("A", a), ("B", b)):
+        if op.data.numel() * op.data.element_size() < op.rows * row_bytes:
+            raise ValueError(f"{name} data holds fewer than {op.rows} x {row_bytes} bytes")
+    scale_kind = nat.BB_LOWP_NVFP4 if kind == "nvfp4" else nat.BB_LOWP_FP8_BLOCK128
+    for name, rows, t in (("A", a.rows, sfa), ("B", b.rows, sfb)):
+        need = int(nat.bench_lib().bb_lowp_scale_bytes(scale_kind, rows, a.k))
+        have = t.numel() * t.element_size()
+        if need > 0 and have < need:
+            raise ValueError(f"{name} scales hold {have} bytes, the kernel reads {need}")
+
+
 class LowpGemmPlan:
     """D (M, N) BF16 = dequant(A) @ dequant(B)^T through the sm_100a
     block-scaled kernel (bb_lowp_plan_create of include/b200bench.h)."""
@@ -197,12 +222,10 @@ class LowpGemmPlan:
             sfa, sfb, gscale = a.atoms, b.atoms, a.tensor_scale * b.tensor_scale
         else:
             sfa, sfb, gscale = a.scales, b.scales, 1.0
-        for t in (a.data, b.data, sfa, sfb):
-            if not t.is_cuda or not t.is_contiguous():
-                raise ValueError("operands must be contiguous CUDA tensors")
-        self.a, self.b, self.d, self._keep = a, b, d, (sfa, sfb)
         self.stream = stream if stream is not None else torch.cuda.current_stream(d.device)
         self._lib = nat.bench_lib()
+        _check_buffers(kind, a, b, d, sfa, sfb, self.stream)
+        self.a, self.b, self.d, self._keep = a, b, d, (sfa, sfb)
         handle = ctypes.c_void_p()
         info = nat.LowpInfo()
         with torch.cuda.device(d.device):
@@ -265,6 +288,9 @@ class CublasLtLowpPlan:
             sfa, sfb, gscale = a.scales, b.scales, 1.0
             if kind != "fp8_tensor_scaled" and not fp8_scales_kmajor:
                 sfa, sfb = sfa.t().contiguous(), sfb.t().contiguous()
+        if not d.is_cuda or d.dtype != torch.bfloat16 or not d.is_contiguous():
+            raise ValueError("D must be a contiguous CUDA bfloat16 tensor")
+        _check_buffers(kind, a, b, d, sfa, sfb, self.stream)
         self._keep = (a, b, sfa, sfb, d)
         handle = ctypes.c_void_p()
         info = nat.CmpInfo()

@@ -34,12 +34,19 @@ def _stream(stream):
     return (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
 
 
+def _check_buffer(buf: torch.Tensor) -> None:
+    if not buf.is_cuda or not buf.is_contiguous():
+        raise ValueError("the buffer must be a contiguous CUDA tensor")
+
+
 def fill_pattern(buf: torch.Tensor, stream=None) -> None:
+    _check_buffer(buf)
     nat.check("bb_fill_pattern", nat.bench_lib().bb_fill_pattern(buf.data_ptr(), buf.numel() * buf.element_size(),
                                                                   _stream(stream)))
 
 
 def fill_uniform_u32(buf: torch.Tensor, seed: int = 0, stream=None) -> None:
+    _check_buffer(buf)
     nat.check("bb_fill_uniform_u32", nat.bench_lib().bb_fill_uniform_u32(
         buf.data_ptr(), buf.numel() * buf.element_size(), seed, _stream(stream)))
 
@@ -55,7 +62,10 @@ class StreamingRun:
             raise ValueError("src must be a contiguous CUDA tensor")
         self.method, self.stages, self.bif_kib, self.row_bytes = method, stages, bif_kib, row_bytes
         self.src = src
-        self.nbytes = int(nbytes if nbytes is not None else src.numel() * src.element_size())
+        have = src.numel() * src.element_size()
+        self.nbytes = int(nbytes if nbytes is not None else have)
+        if not 0 < self.nbytes <= have:
+            raise ValueError(f"nbytes={self.nbytes} must be in (0, {have}], the size of src")
         self.stream = stream if stream is not None else torch.cuda.current_stream(src.device)
         self.info = plan(method, stages, bif_kib, self.nbytes, row_bytes)
         dev = src.device

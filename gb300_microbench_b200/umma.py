@@ -39,6 +39,8 @@ class UmmaProbe:
             raise ValueError(f"operands must be A {(m_of(cta_group), K)} and B {(n, K)}")
         if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or not a.is_cuda or not b.is_cuda:
             raise ValueError("operands must be CUDA bfloat16 tensors")
+        if a.device != b.device:
+            raise ValueError(f"A on {a.device}, B on {b.device}: both must be on one device")
         self.cta_group, self.n, self.depth = cta_group, n, depth
         self.name = kernel_name(cta_group, n, depth)
         self.a, self.b = a.contiguous(), b.contiguous()

@@ -104,7 +104,8 @@ BB_API int bb_gemm_plan_create(int64_t m, int64_t n, int64_t k, int64_t l, const
 /* One launch on the plan's stream (asynchronous). Replaces p35_plan_execute
  * (cublaslt_bridge.cu:949). */
 BB_API int bb_gemm_execute(bb_gemm_plan* plan);
-/* `iterations` back-to-back launches (asynchronous). */
+/* `iterations` back-to-back launches (asynchronous); 0 queues nothing,
+ * a negative count is BB_ERR_ARGUMENT. */
 BB_API int bb_gemm_execute_n(bb_gemm_plan* plan, int iterations);
 /* End-to-end call with HOST buffers: copies a_host/b_host into the plan's
  * device A/B, runs the GEMM and copies C back into c_host, then waits for

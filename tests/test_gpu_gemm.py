@@ -178,6 +178,24 @@ def test_bad_arguments_rejected(cuda_device):
     assert ei.value.status == nat.BB_ERR_ARGUMENT
 
 
+def test_negative_iteration_count_rejected(cuda_device):
+    from gb300_microbench_b200 import _native as nat
+
+    a = torch.zeros(256, 128, dtype=torch.bfloat16, device=cuda_device)
+    b = torch.zeros(256, 128, dtype=torch.bfloat16, device=cuda_device)
+    c = torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda_device)
+    plan = GemmPlan(a, b, c)
+    try:
+        before = plan.launches
+        plan.run(0)
+        with pytest.raises(nat.NativeCallError) as ei:
+            plan.run(-1)
+        assert ei.value.status == nat.BB_ERR_ARGUMENT
+        assert plan.launches == before
+    finally:
+        plan.close()
+
+
 @pytest.mark.parametrize("mnk", [(4096, 4096, 1024), (16384, 512, 1024), (512, 16384, 1024), (2304, 2048, 4096),
                                  (640, 768, 2048), (32768, 512, 4096), (256, 2560, 3072)])
 def test_split_tail_exact(cuda_device, mnk, monkeypatch):

@@ -114,6 +114,22 @@ def test_argument_errors(cuda_device):
         a2 = _nvfp4_exact_operand(128, 128, gen).to(cuda_device)
         b2 = _nvfp4_exact_operand(256, 128, gen).to(cuda_device)
         lowp.LowpGemmPlan("nvfp4", a2, b2, torch.empty(128, 256, dtype=torch.bfloat16, device=cuda_device))
+    # FP8 block scales smaller than the (R/128, K/128) grid the kernel reads
+    q = torch.zeros(256, 256, dtype=torch.uint8, device=cuda_device)
+    short = lowp.Fp8BlockOperand.from_parts(q, torch.ones(1, 1, device=cuda_device))
+    full = lowp.Fp8BlockOperand.from_parts(q, torch.ones(2, 2, device=cuda_device))
+    dd = torch.empty(256, 256, dtype=torch.bfloat16, device=cuda_device)
+    for x, y in ((short, full), (full, short)):
+        with pytest.raises(ValueError, match="scales hold"):
+            lowp.LowpGemmPlan("fp8_block128", x, y, dd)
+    plan = lowp.LowpGemmPlan("nvfp4", a, b, torch.empty(128, 256, dtype=torch.bfloat16, device=cuda_device))
+    try:
+        with pytest.raises(nat.NativeCallError) as ei:
+            plan.run(-1)
+        assert ei.value.status == nat.BB_ERR_ARGUMENT
+        assert plan.launches == 0
+    finally:
+        plan.close()
 
 
 def test_config4_size_checksums(cuda_device):
