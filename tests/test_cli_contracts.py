@@ -123,8 +123,35 @@ def test_our_rows_pass_reference_validators():
 def test_committed_result_csvs_pass_campaign_validators():
     rc = _ref_module("scripts/run_campaign.py", "ref_rc")
     for name, validator in (("memory_paths_reference.csv", rc.validate_memory),
-                            ("umma_reference.csv", rc.validate_umma)):
+                            ("umma_reference.csv", rc.validate_umma),
+                            ("gemm_comparison.csv", rc.validate_gemm)):
         path = ROOT / "results" / name
         rows = list(csv.DictReader(path.open()))
         n = validator(path, commit=rows[0]["git_commit"], gpu_uuid=rows[0]["gpu_uuid"])
         assert n == len(rows)
+
+
+def test_committed_result_csvs_feed_reference_analysis(tmp_path):
+    """The reference's cross-campaign statistics (analysis/analyze.py:484-886)
+    and figures (:1099) consume the committed B200 CSVs unchanged. The three
+    campaign records are the same CSVs three times (one campaign was run
+    here); counter-derived figures need ncu profiles and read as absent."""
+    an = _ref_module("analysis/analyze.py", "ref_analyze")
+
+    def rows(name):
+        return list(csv.DictReader((ROOT / "results" / name).open()))
+
+    records = [{"campaign_id": f"c{i}", "manifest": {}, "memory": rows("memory_paths_reference.csv"),
+                "umma": rows("umma_reference.csv"), "gemm": rows("gemm_comparison.csv"),
+                "profiles": {"memory_paths": {}, "umma_throughput": {}, "gemm_comparison": {}}}
+               for i in range(3)]
+    mem_rows, mem = an.memory_analysis(records)
+    umma_rows, umma = an.umma_analysis(records)
+    gemm_rows, gemm = an.gemm_analysis(records)
+    assert len(mem["configurations"]) == 18  # {ldgsts, tma} x stages {2,4,8} x {16,32,64} KiB
+    assert len(umma["configurations"]) == 24  # {1sm, 2sm} x N {64,128,256} x depth {4,16,64,256}
+    assert [s["shape_index"] for s in gemm["shapes"]] == [1, 2, 3, 4, 5]
+    assert all(s["best_cutedsl_variant_consensus"] for s in gemm["shapes"])
+    assert mem_rows and umma_rows and gemm_rows
+    an.figures(tmp_path, mem, umma, gemm)
+    assert any(p.suffix == ".svg" for p in (tmp_path / "figures").iterdir())
