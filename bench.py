@@ -85,7 +85,7 @@ def committed_traffic():
 
 class ClockSampler:
     """Samples the SM clock and the throttle reasons through NVML every
-    ~2 ms on a background thread while the timed region runs."""
+    0.5 ms on a background thread while the timed region runs."""
 
     REASONS = {
         "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
