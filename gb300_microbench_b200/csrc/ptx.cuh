@@ -224,17 +224,22 @@ __device__ __forceinline__ bool bb_wait_warp(uint32_t addr, uint32_t parity, int
   };
   bool ok = probe();
   if (!ok) {
+    // The budget and the abort word (a global load) are checked every 8th
+    // probe only: a phase that completes during those checks is seen late.
     const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
     while (true) {
       if (probe()) {
         ok = true;
         break;
       }
-      if (globaltimer_ns() - t0 > budget_ns) {
-        if (status && (threadIdx.x % 32) == 0) atomicCAS(status, 0, code);
-        break;
+      if ((++spins & 7u) == 0) {
+        if (globaltimer_ns() - t0 > budget_ns) {
+          if (status && (threadIdx.x % 32) == 0) atomicCAS(status, 0, code);
+          break;
+        }
+        if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) break;
       }
-      if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) break;
     }
   }
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;

@@ -197,10 +197,17 @@ __global__ void wait_timeout_kernel(int64_t budget_ns, int* status) {
     bb::fence_mbarrier_init_cluster();
   }
   __syncthreads();
+  // Nothing ever arrives on `bar`: every wait form must give up after its
+  // budget and record it. Status slots: [0] single-thread wait, [1] warp-wide
+  // spinning wait, [2] warp-wide wait with the suspend hint.
   if (threadIdx.x == 0) {
-    // Nothing ever arrives on `bar`: the wait must give up and record it.
     bb::bb_wait(bb::smem_u32(&bar), 0, status, bb::kDevTimeoutTest, false, static_cast<uint64_t>(budget_ns));
   }
+  __syncwarp();
+  bb::bb_wait_warp<false, false>(bb::smem_u32(&bar), 0, status + 1, bb::kDevTimeoutTest, false,
+                                 static_cast<uint64_t>(budget_ns));
+  bb::bb_wait_warp<false, true>(bb::smem_u32(&bar), 0, status + 2, bb::kDevTimeoutTest, false,
+                                static_cast<uint64_t>(budget_ns));
   __syncthreads();
 }
 

@@ -227,9 +227,12 @@ BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int 
 BB_API const char* bb_umma_kernel_name(int cta_group, int n, int depth);
 
 /* ======================================================== fault injection
- * Launches a one-CTA kernel that waits on an mbarrier nothing will complete,
- * with a wait budget of `budget_ns`; the kernel records BB timeout code in
- * *status and returns. Exercises the bounded-wait path without faulting or
+ * Launches a one-warp kernel that waits on an mbarrier nothing will complete,
+ * with a wait budget of `budget_ns` per wait, in three forms: one thread
+ * (status[0]), the whole warp spinning (status[1]) and the whole warp with
+ * the suspend hint (status[2]); each records the BB timeout code in its
+ * status int (`status` points at three ints) and the kernel returns after
+ * about 3 x budget_ns. Exercises the bounded-wait paths without faulting or
  * hanging the GPU. No counterpart in the reference (its waits are unbounded:
  * memory_paths/tma.cu:399-403). */
 BB_API int bb_test_wait_timeout(int64_t budget_ns, int* status, void* stream);

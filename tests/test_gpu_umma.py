@@ -38,13 +38,14 @@ def test_random_operands(cuda_device, cta_group, n, depth):
 
 
 def test_wait_timeout_is_reported_not_hung(cuda_device):
-    """A wait that nothing completes gives up after its budget and reports
-    through the status word; the context stays usable afterwards."""
+    """Waits that nothing completes (single thread, warp-wide spinning,
+    warp-wide with the suspend hint) give up after their budget and report
+    through their status words; the context stays usable afterwards."""
     from gb300_microbench_b200 import _native as nat
 
-    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    status = torch.zeros(3, dtype=torch.int32, device=cuda_device)
     nat.call("bb_test_wait_timeout", 2_000_000, status.data_ptr(), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    assert int(status.item()) == 0x106
+    assert status.tolist() == [0x106, 0x106, 0x106]
     x = torch.ones(4, device=cuda_device)
     assert float((x * 2).sum().item()) == 8.0
