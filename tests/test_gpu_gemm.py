@@ -68,6 +68,48 @@ def test_batched_l2(cuda_device, variant):
         assert torch.equal(c[i], ref)
 
 
+@pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("mnkl", [(300, 264, 200, 3), (129, 8, 72, 2)])
+def test_batched_ragged(cuda_device, variant, mnkl):
+    """Batches whose every extent is ragged against the tiles: each batch
+    entry must be exact and no entry may write into another's rows."""
+    m, n, k, l = mnkl
+    a, b = inputs.reference_mode_operands(m, n, k, l=l)
+    c = _run(a, b, torch.float32, variant, cuda_device)
+    assert torch.isfinite(c).all(), "unwritten (NaN) output elements"
+    for i in range(l):
+        assert torch.equal(c[i], oracle.gemm_reference_fp32(a[i], b[i]))
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("mnk", [(1, 8, 8), (1, 16, 64), (7, 8, 72), (129, 264, 8), (2, 520, 136)])
+def test_minimal_extents_exact(cuda_device, variant, mnk):
+    """The smallest legal extents (M = 1, N = 8, K = 8) and shapes below one
+    tile in every dimension: the tensor maps' zero fill and the clipped
+    stores must give the exact product and write every element of C."""
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0], b[0]
+    c = _run(a, b, torch.float32, variant, cuda_device)
+    assert torch.isfinite(c).all(), "unwritten (NaN) output elements"
+    assert torch.equal(c, oracle.gemm_reference_fp32(a, b))
+    cb = _run(a, b, torch.bfloat16, variant, cuda_device)
+    assert torch.equal(cb, oracle.gemm_reference_fp32(a, b).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("variant", ["tuned", "persistent_1cta"])
+@pytest.mark.parametrize("mnk", [(256, 256, 16384), (128, 64, 32768)])
+def test_long_k_exact(cuda_device, variant, mnk):
+    """Long reductions (256-512 k-blocks; the tuned variant splits the single
+    tile along K and exchanges partials): integer products stay exact in
+    FP32, so any dropped or doubled k-block shows."""
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0], b[0]
+    c = _run(a, b, torch.float32, variant, cuda_device)
+    assert torch.equal(c, oracle.gemm_reference_fp32(a, b))
+
+
 @pytest.mark.parametrize("variant", ["tuned", "persistent_2cta"])
 def test_full_size_4096_baseline(cuda_device, variant):
     """Config 0 at full size: 4096^3, N(0,1) seed 0, BF16 C."""

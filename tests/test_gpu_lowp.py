@@ -65,7 +65,7 @@ def _run(kind, a, b, dev):
 
 
 EXACT_SHAPES = [(128, 256, 256), (256, 512, 512), (384, 256, 1024), (200, 264, 512), (1024, 768, 768),
-                (520, 136, 256)]
+                (520, 136, 256), (1, 8, 256), (130, 24, 256)]  # the last two: minimal and sub-tile extents
 
 
 @pytest.mark.parametrize("cta_group", ["1", "2"])
