@@ -73,3 +73,21 @@ def test_full_size_4gib_checksum_of_checksums(cuda_device):
         assert int(got) == want, method
     del buf
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("method,row_bytes,nbytes", [("ldgsts", 256, 16), ("ldgsts", 256, 4096),
+                                                     ("ldgsts", 256, 8192 + 16), ("tma", 256, 256),
+                                                     ("tma", 128, 3 * 128), ("tma", 128, 8192 + 128)])
+def test_tiny_buffers(cuda_device, method, row_bytes, nbytes):
+    """Buffers of one short tile or barely more: most CTAs get no tile, the
+    one or two that do stop at the buffer's end (checksums bit-exact)."""
+    buf = torch.empty(nbytes // 4, dtype=torch.int32, device=cuda_device)
+    streaming.fill_uniform_u32(buf, seed=3)
+    words = oracle.uniform_u32(nbytes // 4, seed=3)
+    for stages in (2, 4):
+        run = streaming.StreamingRun(method, stages, 16, buf, row_bytes=row_bytes)
+        run.run(passes=2)
+        got = np.array(run.checksums(), dtype=np.uint32)
+        want = oracle.copy_checksums(words, run.info["stage_bytes"], run.info["grid_ctas"], 2)
+        assert np.array_equal(got, want), (stages, run.info)
+        run.check_status()
