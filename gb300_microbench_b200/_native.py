@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_uint64, c_ulonglong, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"

@@ -34,7 +34,6 @@ import csv
 import hashlib
 import io
 import math
-import os
 import subprocess
 import sys
 import time

@@ -13,7 +13,6 @@ from pathlib import Path
 
 import pytest
 
-from gb300_microbench_b200.cli import common as cm
 from gb300_microbench_b200.cli import gemm_comparison as gc
 from gb300_microbench_b200.cli import memory_paths as mp
 from gb300_microbench_b200.cli import umma as um

@@ -9,7 +9,6 @@ Two kinds of cases per format:
   the dequantised inputs <= 2e-2 (the configuration's check); observed errors
   are BF16 output rounding, about 2e-3.
 """
-import numpy as np
 import pytest
 import torch
 
