@@ -589,7 +589,6 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
         named_bar_sync(1, kEpiThreads);
         const bool peers_ok = epi_flag[0] != 0;
         if (peers_ok) {
-#pragma unroll 1
           const int own0 = j * slice > wc0 ? j * slice : wc0;
           const int own1 = (j + 1) * slice < wc0 + C::WARP_COLS ? (j + 1) * slice : wc0 + C::WARP_COLS;
           for (int c = own0 / ncols; c < own1 / ncols; ++c) {
