@@ -1,9 +1,10 @@
-"""Multi-GPU GEMM sweep: the five frozen shapes (gemm_comparison.py:116-122)
+"""Multi-GPU GEMM sweep: the five frozen shapes (gemm_comparison.py:116-122, or --shapes)
 row-sharded over the ranks of one node, B replicated, in baseline mode
 (N(0,1) seed-0 BF16 operands, BF16 C). One process per GPU:
 
     python -m torch.distributed.run --nproc-per-node P --master-addr 127.0.0.1 \\
         -m gb300_microbench_b200.cli.multigpu [--iterations N] [--warmup-iterations N] [--output FILE]
+        [--shapes MxNxK,...]
 
 Each rank times its own block with CUDA events (N back-to-back launches
 after warm-up); the shape's time is the max over ranks and the aggregate
@@ -32,7 +33,18 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup-iterations", type=int, default=5)
     ap.add_argument("--variant", default="tuned")
     ap.add_argument("--output", default="-")
+    ap.add_argument("--shapes", default=None,
+                    help="comma-separated MxNxK list instead of the five frozen shapes")
     args = ap.parse_args(sys.argv[1:] if argv is None else argv)
+    shapes = SHAPES
+    if args.shapes:
+        try:
+            shapes = tuple(tuple(int(v) for v in item.split("x")) for item in args.shapes.split(","))
+            if any(len(t) != 3 or min(t) < 1 for t in shapes):
+                raise ValueError
+        except ValueError:
+            cm.eprint(f"multigpu: --shapes wants MxNxK[,MxNxK...] with positive extents, got {args.shapes!r}")
+            return cm.EXIT_USAGE
 
     import torch
     import torch.distributed as dist
@@ -50,7 +62,7 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", device_id=dev)
     rows_out = []
     try:
-        for (m, n, k) in SHAPES:
+        for (m, n, k) in shapes:
             a_cpu, b_cpu = baseline_mode_operands(m, n, k)
             shards = [row_shard(m, world, r, granule=128) for r in range(world)]
             me = shards[rank]
@@ -58,23 +70,30 @@ def main(argv=None) -> int:
             b = b_cpu.to(dev)
             c = torch.empty(me.rows, n, dtype=torch.bfloat16, device=dev)
             stream = torch.cuda.Stream(device=dev)
-            plan = GemmPlan(a, b, c, variant=args.variant, stream=stream)
-            plan.run(args.warmup_iterations)
-            plan.synchronize()
+            # A rank whose block is empty (fewer 128-row granules than ranks)
+            # launches nothing but still joins every collective.
+            plan = GemmPlan(a, b, c, variant=args.variant, stream=stream) if me.rows > 0 else None
+            if plan:
+                plan.run(args.warmup_iterations)
+                plan.synchronize()
             if world > 1:
                 dist.barrier()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            plan.run(args.iterations)
-            e1.record(stream)
-            e1.synchronize()
-            ms = torch.tensor([e0.elapsed_time(e1) / args.iterations], dtype=torch.float64, device=dev)
+            local_ms = 0.0
+            if plan:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                plan.run(args.iterations)
+                e1.record(stream)
+                e1.synchronize()
+                local_ms = e0.elapsed_time(e1) / args.iterations
+            ms = torch.tensor([local_ms], dtype=torch.float64, device=dev)
             if world > 1:
                 dist.all_reduce(ms, op=dist.ReduceOp.MAX)
             ms = float(ms.item())
             full = gather_rows(c, shards) if world > 1 else c
-            info = plan.info
-            plan.close()
+            info = plan.info if plan else None
+            if plan:
+                plan.close()
             if rank == 0:
                 torch.backends.cuda.matmul.allow_tf32 = False
                 ref = torch.matmul(a_cpu.to(dev).float(), b.float().t())

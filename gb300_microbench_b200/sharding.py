@@ -27,14 +27,19 @@ class RowShard:
 
 def row_shard(m: int, world: int, rank: int, granule: int = 1) -> RowShard:
     """Contiguous, balanced row blocks; block sizes are multiples of
-    `granule` except possibly the last."""
+    `granule` except possibly the last. With fewer granules than ranks the
+    lowest ranks hold them and the rest get empty blocks, so rank 0 always
+    holds rows when m > 0."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"rank {rank} of world {world} is invalid")
     if m < 0 or granule < 1:
         raise ValueError("m must be >= 0 and granule >= 1")
     units = -(-m // granule)
-    u0 = rank * units // world
-    u1 = (rank + 1) * units // world
+    if units < world:
+        u0, u1 = min(rank, units), min(rank + 1, units)  # one granule each to the lowest ranks
+    else:
+        u0 = rank * units // world
+        u1 = (rank + 1) * units // world
     row0 = min(u0 * granule, m)
     row1 = min(u1 * granule, m)
     return RowShard(rank, world, row0, row1 - row0)

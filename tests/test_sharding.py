@@ -24,6 +24,8 @@ def test_row_shard_partitions_rows(m, world, granule):
     assert covered == list(range(m))
     sizes = [s.rows for s in shards]
     assert max(sizes) - min(sizes) <= granule
+    if m > 0:
+        assert shards[0].rows > 0  # rank 0 (which writes the results) always holds rows
 
 
 def _free_port() -> int:
@@ -32,12 +34,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, fail_rank, results):
+def _worker(rank, world, port, fail_rank, results, m_rows=300):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     try:
         g = torch.Generator().manual_seed(0)
-        a = torch.randn(300, 64, generator=g)
+        a = torch.randn(m_rows, 64, generator=g)
         b = torch.randn(40, 64, generator=g)
         if rank == fail_rank:
             raise RuntimeError("injected rank failure before the validation all-gather")
@@ -53,11 +55,11 @@ def _worker(rank, world, port, fail_rank, results):
             pass
 
 
-def _run(world, fail_rank=-1):
+def _run(world, fail_rank=-1, m_rows=300):
     port = _free_port()
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.spawn(_worker, args=(world, port, fail_rank, results), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, port, fail_rank, results, m_rows), nprocs=world, join=True)
         return dict(results)
 
 
@@ -71,3 +73,10 @@ def test_failed_rank_surfaces_on_every_rank():
     res = _run(2, fail_rank=1)
     assert res[1].startswith("error: injected")
     assert res[0].startswith("error")  # the survivor's all-gather ends with an error, not a hang
+
+
+def test_gloo_sharded_gemm_with_empty_ranks():
+    """40 rows in 32-row granules over 3 ranks: two granules, so rank 2's
+    block is empty; it still joins the all-gather and C reassembles."""
+    res = _run(3, m_rows=40)
+    assert res == {r: "ok" for r in range(3)}
