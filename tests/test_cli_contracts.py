@@ -154,3 +154,11 @@ def test_committed_result_csvs_feed_reference_analysis(tmp_path):
     assert mem_rows and umma_rows and gemm_rows
     an.figures(tmp_path, mem, umma, gemm)
     assert any(p.suffix == ".svg" for p in (tmp_path / "figures").iterdir())
+
+
+@pytest.mark.parametrize("bad", ["12x3", "0x8x8", "axbxc", "8x8x8,"])
+def test_multigpu_shapes_usage_errors(bad, capsys):
+    from gb300_microbench_b200.cli import multigpu
+
+    assert multigpu.main(["--shapes", bad]) == 2
+    assert "--shapes" in capsys.readouterr().err
