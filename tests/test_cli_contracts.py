@@ -125,7 +125,7 @@ def test_committed_result_csvs_pass_campaign_validators():
                             ("umma_reference.csv", rc.validate_umma),
                             ("gemm_comparison.csv", rc.validate_gemm)):
         path = ROOT / "results" / name
-        rows = list(csv.DictReader(path.open()))
+        rows = list(csv.DictReader(path.read_text().splitlines()))
         n = validator(path, commit=rows[0]["git_commit"], gpu_uuid=rows[0]["gpu_uuid"])
         assert n == len(rows)
 
@@ -138,7 +138,7 @@ def test_committed_result_csvs_feed_reference_analysis(tmp_path):
     an = _ref_module("analysis/analyze.py", "ref_analyze")
 
     def rows(name):
-        return list(csv.DictReader((ROOT / "results" / name).open()))
+        return list(csv.DictReader((ROOT / "results" / name).read_text().splitlines()))
 
     records = [{"campaign_id": f"c{i}", "manifest": {}, "memory": rows("memory_paths_reference.csv"),
                 "umma": rows("umma_reference.csv"), "gemm": rows("gemm_comparison.csv"),
