@@ -56,6 +56,13 @@ int build_maps(Plan& pl) {
     int rc = encode_tiled(&pl.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, pl.b, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (rc != BB_OK) return rc;
+    if (pl.narrow_tiles > 0) {
+      // Half-height boxes of B for the narrow tail's half-width items.
+      const uint32_t half_box[3] = {64, static_cast<uint32_t>(pl.b_rows / 2), 1};
+      rc = encode_tiled(&pl.tm_b_half, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, pl.b, dims, strides, half_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+      if (rc != BB_OK) return rc;
+    }
   }
   {
     const bool f32 = pl.c_dtype == BB_DTYPE_F32;
@@ -171,7 +178,7 @@ int init_pipe(bb_gemm_plan* plan) {
     q.c_src = p.c_src ? static_cast<const uint8_t*>(p.c_src) + static_cast<size_t>(r) * p.n * es : nullptr;
     rc = gemm::plan_init(q, p.variant, dev.sm_count);
     if (rc == BB_OK) rc = gemm::build_maps(q);
-    if (rc == BB_OK && q.sk_parts > 0) {
+    if (rc == BB_OK && q.sk_tiles > 0) {
       rc = check_cuda(cudaMalloc(&q.partials, q.partial_floats * sizeof(float)), "cudaMalloc(pipe partials)");
       if (rc == BB_OK) rc = check_cuda(cudaMalloc(&q.counters, q.counter_ints * sizeof(int)), "cudaMalloc(pipe counters)");
       if (rc == BB_OK) rc = check_cuda(cudaMemset(q.counters, 0, q.counter_ints * sizeof(int)), "cudaMemset(pipe counters)");
@@ -300,7 +307,7 @@ BB_API int bb_gemm_plan_create(int64_t m, int64_t n, int64_t k, int64_t l, const
     if (rc == BB_OK) rc = gemm::build_maps(p);
     if (rc == BB_OK) rc = check_cuda(cudaMalloc(&h->status_dev, sizeof(int)), "cudaMalloc(status)");
     if (rc == BB_OK) rc = check_cuda(cudaMemset(h->status_dev, 0, sizeof(int)), "cudaMemset(status)");
-    if (rc == BB_OK && p.sk_parts > 0) {
+    if (rc == BB_OK && p.sk_tiles > 0) {
       // Stream-K workspace, owned by the plan (as the reference bridge owns
       // its cuBLASLt workspace). Counters start at zero and are reset by the
       // kernel after each use.

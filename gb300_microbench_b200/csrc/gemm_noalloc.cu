@@ -2,29 +2,32 @@
 // device memory, e.g. code running where cudaMalloc is off limits (inside a
 // custom allocator's own callbacks, a plugin host that owns the whole device
 // heap, or a CUDA-graph-building framework that forbids allocation while it
-// records). It is the same kernel as bb_gemm_plan_create/bb_gemm_execute
-// with the tuned variant; only where its scratch lives differs.
+// records). It runs the kernel of bb_gemm_plan_create/bb_gemm_execute with
+// the tuned variant; only where its scratch lives differs.
 //
-// Scratch: the GEMM's split-tail workspace (partial slices, arrival
-// counters) and its device status word live in one file-scope __device__
-// array of kScratchBytes (16 MiB + 64 KiB). Every GPU that loads this
-// library holds that array until the process exits. The tuned split tail
-// needs at most rem * (s - 1) * 256 KiB of partials with rem * s <= 74
-// clusters and s in {2, 4} (13.5 MiB at most), so it always fits; a problem
-// that would need more is rejected with BB_ERR_ARGUMENT all the same.
-// Problems without a split tail need only the status word.
+// Scratch: the GEMM's stream-K workspace (partial tiles, k-block counters)
+// and its device status word live in one file-scope __device__ array of
+// kScratchBytes (37 MiB + 64 KiB). Every GPU that loads this library holds
+// that array until the process exits. The partial tiles take two slots per
+// cluster: 2 x 74 pairs x 2 CTAs x 128 x 256 FP32 = 37 MiB on a 148-SM B200,
+// the most any tuned plan needs there (only tiles up to 256 wide get a
+// stream-K region; 148 single CTAs with 128-wide tiles need half of it). A
+// problem whose workspace would not fit (a device with more SMs) is refused
+// with BB_ERR_ARGUMENT.
 //
 // Host code cannot use the array's name as a device address (in host code
-// it names a host-side stand-in), so the first call on each device, with
-// that device current, resolves the address with cudaGetSymbolAddress and
-// caches it. That first call should therefore come before any stream
-// capture. Every call then clears the status word and the counters with
-// cudaMemsetAsync on the caller's stream and launches the kernel; no call
-// allocates or frees device memory. With wait != 0 the call also
-// synchronises the stream and returns BB_ERR_TIMEOUT when a device-side wait
-// gave up; with wait == 0 it returns as soon as the work is queued. All calls share the one array, which
-// keeps the last call's contents: calls that overlap on the GPU (different
-// streams without ordering between them) race on it.
+// it names a host-side stand-in), so the first call in each CUDA context
+// (normally a device's primary context), with that context current,
+// resolves the address with cudaGetSymbolAddress and caches it per context.
+// That first call should therefore come before any stream capture. Every
+// call then clears the status word and the counters with cudaMemsetAsync on
+// the caller's stream and launches the kernel; no call allocates or frees
+// device memory. With wait != 0 the call also synchronises the stream and
+// returns BB_ERR_TIMEOUT when a device-side wait gave up; with wait == 0 it
+// returns as soon as the work is queued and gives up that report (the next
+// call clears the status word). All calls share the one array, which keeps
+// the last call's contents: calls that overlap on the GPU (different streams
+// without ordering between them) race on it.
 #include <atomic>
 #include <mutex>
 
@@ -38,31 +41,72 @@ namespace gemm_noalloc {
 
 constexpr size_t kStatusBytes = 256;
 constexpr size_t kCounterBytes = 64 * 1024 - kStatusBytes;
-constexpr size_t kPartialBytes = 16u << 20;
+constexpr size_t kPartialBytes = 37u << 20;
 constexpr size_t kScratchBytes = kStatusBytes + kCounterBytes + kPartialBytes;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
+// Device addresses of g_scratch, one per CUDA context (each context that
+// loads the module has its own copy of the array).
+constexpr int kMaxContexts = 64;
 std::mutex g_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
+void* g_ctx_key[kMaxContexts] = {};
+void* g_scratch_addr[kMaxContexts] = {};
 
-// Resolves the device address of g_scratch for the current device, once.
+using CtxGetCurrentFn = int (*)(void**);
+
+// The current driver context (CUcontext) as an opaque key; null if none.
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+  });
+  void* ctx = nullptr;
+  if (fn && fn(&ctx) != 0) ctx = nullptr;
+  return ctx;
+}
+
+// Resolves the device address of g_scratch in the current context, once.
 int scratch_address(int device, unsigned char** out) {
-  if (device < 0 || device >= kMaxDevices) {
-    set_error("bb_gemm_run_noalloc: device index %d out of range", device);
-    return BB_ERR_UNSUPPORTED;
+  // The context current to this thread is the one the launch will use. If
+  // none is current yet, bind the device's primary context (since CUDA 12
+  // cudaSetDevice initialises it).
+  void* ctx = current_context();
+  if (!ctx) {
+    BB_CUDA_TRY(cudaSetDevice(device));
+    ctx = current_context();
+  }
+  if (!ctx) {
+    set_error("bb_gemm_run_noalloc: no current CUDA context");
+    return BB_ERR_CUDA;
   }
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch_addr[device]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      return check_cuda(e == cudaSuccess ? cudaErrorInvalidSymbol : e, "cudaGetSymbolAddress(noalloc scratch)");
+  int slot = -1;
+  for (int i = 0; i < kMaxContexts; ++i) {
+    if (g_ctx_key[i] == ctx) {
+      *out = static_cast<unsigned char*>(g_scratch_addr[i]);
+      return BB_OK;
     }
-    g_scratch_addr[device] = ptr;
+    if (slot < 0 && g_ctx_key[i] == nullptr) slot = i;
   }
-  *out = static_cast<unsigned char*>(g_scratch_addr[device]);
+  if (slot < 0) {
+    set_error("bb_gemm_run_noalloc: more than %d CUDA contexts", kMaxContexts);
+    return BB_ERR_UNSUPPORTED;
+  }
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
+  if (e != cudaSuccess || ptr == nullptr) {
+    return check_cuda(e == cudaSuccess ? cudaErrorInvalidSymbol : e, "cudaGetSymbolAddress(noalloc scratch)");
+  }
+  g_ctx_key[slot] = ctx;
+  g_scratch_addr[slot] = ptr;
+  *out = static_cast<unsigned char*>(ptr);
   return BB_OK;
 }
 
@@ -87,8 +131,12 @@ extern "C" BB_API int bb_gemm_run_noalloc(int64_t m, int64_t n, int64_t k, int64
       set_error("bb_gemm_run_noalloc: C must be BF16 or FP32");
       return BB_ERR_UNSUPPORTED;
     }
-    if (k % 8 != 0 || (c_dtype == BB_DTYPE_BF16 && n % 8 != 0) || (c_dtype == BB_DTYPE_F32 && n % 4 != 0)) {
-      set_error("bb_gemm_run_noalloc: K must be a multiple of 8 and N keep C rows 16-byte aligned");
+    if (k % 8 != 0) {
+      set_error("bb_gemm_run_noalloc: K=%lld must be a multiple of 8 (16-byte TMA row stride)", (long long)k);
+      return BB_ERR_ARGUMENT;
+    }
+    if ((c_dtype == BB_DTYPE_BF16 && n % 8 != 0) || (c_dtype == BB_DTYPE_F32 && n % 4 != 0)) {
+      set_error("bb_gemm_run_noalloc: N=%lld breaks the 16-byte row stride of C", (long long)n);
       return BB_ERR_ARGUMENT;
     }
     DeviceInfo dev;
@@ -114,9 +162,9 @@ extern "C" BB_API int bb_gemm_run_noalloc(int64_t m, int64_t n, int64_t k, int64
     const size_t counter_bytes = static_cast<size_t>(p.counter_ints) * sizeof(int);
     if (partial_bytes > na::kPartialBytes || counter_bytes > na::kCounterBytes) {
       set_error(
-          "bb_gemm_run_noalloc: this problem's split tail needs %zu bytes of partial storage and %zu bytes of "
-          "counters; the static scratch holds at most %zu and %zu",
-          partial_bytes, counter_bytes, na::kPartialBytes, na::kCounterBytes);
+          "bb_gemm_run_noalloc: this problem's stream-K workspace needs %zu bytes of partial tiles and %zu bytes "
+          "of counters on this device (%d SMs); the static scratch holds at most %zu and %zu",
+          partial_bytes, counter_bytes, dev.sm_count, na::kPartialBytes, na::kCounterBytes);
       return BB_ERR_ARGUMENT;
     }
     rc = gemm::build_maps(p);
@@ -127,7 +175,7 @@ extern "C" BB_API int bb_gemm_run_noalloc(int64_t m, int64_t n, int64_t k, int64
                      ? reinterpret_cast<float*>(scratch + na::kStatusBytes + na::kCounterBytes)
                      : nullptr;
     // The status word and the counters must start at zero; the partial
-    // slices are always written before they are read.
+    // tiles are always written before they are read.
     BB_CUDA_TRY(cudaMemsetAsync(scratch, 0, na::kStatusBytes + counter_bytes, p.stream));
     // Ordered after the memset by plain stream order.
     p.pdl = false;

@@ -19,6 +19,7 @@ struct Plan {
   int variant = 0;
   cudaStream_t stream = nullptr;
   CUtensorMap tm_a{}, tm_b{}, tm_c{};
+  CUtensorMap tm_b_half{};  // B with half-height boxes (narrow tail items)
   int threads = 0;
   int cg = 1, tile_m = 0, tile_n = 0, stages = 0, smem_bytes = 0, tmem_cols = 0, b_rows = 0, epi_cols = 0;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, k_blocks = 0, group_m = 8, max_active_clusters = 0, grid = 0;
@@ -26,8 +27,10 @@ struct Plan {
   bool stream_k = false;
   bool pdl = true;           // launch with programmatic stream serialisation
   int dp_tiles = 0;          // tiles computed whole (data-parallel)
-  int sk_parts = 0;          // K parts per split tail tile (0: no split tail)
-  int64_t partial_floats = 0;  // workspace the split-tail tail needs
+  int narrow_tiles = 0;      // tail tiles computed as two half-width items
+  int sk_tiles = 0;          // tiles of the stream-K region (0: none)
+  int sk_snap = 0;           // k-blocks within which a range end snaps to a tile edge
+  int64_t partial_floats = 0;  // workspace the stream-K fix-up needs
   int64_t counter_ints = 0;
   float* partials = nullptr;
   int* counters = nullptr;

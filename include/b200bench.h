@@ -131,16 +131,17 @@ BB_API int bb_gemm_destroy(bb_gemm_plan* plan);
 /* GEMM for callers that cannot allocate device memory (code that runs where
  * cudaMalloc is not allowed, such as inside an allocator's callbacks or a
  * host that owns the whole device heap). No counterpart in the reference.
- * Same kernel and results as the tuned variant of bb_gemm_plan_create /
- * bb_gemm_execute, but no plan and no allocation: its scratch (the split-tail
- * partial slices and counters, and the status word) is a static 16 MiB +
- * 64 KiB device array that every GPU loading this library keeps until exit.
- * Problems whose split tail needs more than 16 MiB of partial storage are
- * rejected with BB_ERR_ARGUMENT. The first call on a device resolves the
+ * The tuned variant's kernel of bb_gemm_plan_create / bb_gemm_execute, but no
+ * plan and no allocation: its scratch (the stream-K partial tiles and
+ * counters, and the status word) is a static 37 MiB + 64 KiB device array
+ * that every GPU loading this library keeps until exit: the most a tuned plan
+ * needs on a 148-SM B200. A problem whose workspace would not fit (a device
+ * with more SMs) is refused with BB_ERR_ARGUMENT. The first call in a CUDA context resolves the
  * array's address (cudaGetSymbolAddress), so make it before any stream
  * capture. Calls share the array: calls that overlap on the GPU race. With
  * wait != 0 the call synchronises `stream` and reports a device-side wait
- * timeout as BB_ERR_TIMEOUT; with wait == 0 it only queues the work. */
+ * timeout as BB_ERR_TIMEOUT; with wait == 0 it only queues the work and
+ * gives up that report. */
 BB_API int bb_gemm_run_noalloc(int64_t m, int64_t n, int64_t k, int64_t l, const void* a, const void* b, void* c,
                                int c_dtype, void* stream, int wait);
 

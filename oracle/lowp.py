@@ -53,17 +53,30 @@ def unpack_fp4(packed: np.ndarray) -> np.ndarray:
 
 
 def unpack_scale_atoms(atoms: np.ndarray, rows: int, k: int) -> np.ndarray:
-    """Atoms (flat bytes, [rb][K/64][512]) -> (rows, K/16) scale bytes."""
+    """Atoms (flat bytes, [rb][K/64][512]) -> (rows, K/16) scale bytes.
+
+    Byte (r % 32) * 16 + (r // 32) * 4 + j of atom (rb, g) is scale j of row
+    rb * 128 + r in K group g: viewed as [rb][g][r % 32][r // 32][j]."""
     atoms = np.asarray(atoms, dtype=np.uint8).reshape(-1)
     rb = -(-rows // 128)
     kg = k // 64
-    out = np.empty((rb * 128, kg * 4), dtype=np.uint8)
-    for r in range(rb * 128):
+    v = atoms[: rb * kg * 512].reshape(rb, kg, 32, 4, 4)
+    out = v.transpose(0, 3, 2, 1, 4).reshape(rb * 128, kg * 4)
+    return np.ascontiguousarray(out[:rows])
+
+
+def unpack_scale_atoms_bytewise(atoms: np.ndarray, rows: int, k: int) -> np.ndarray:
+    """The same unpacking one byte at a time (small cases: cross-checks the
+    vectorised form)."""
+    atoms = np.asarray(atoms, dtype=np.uint8).reshape(-1)
+    kg = k // 64
+    out = np.empty((rows, kg * 4), dtype=np.uint8)
+    for r in range(rows):
         blk, rr = divmod(r, 128)
         for g in range(kg):
-            base = (blk * kg + g) * 512 + (rr % 32) * 16 + (rr // 32) * 4
-            out[r, 4 * g:4 * g + 4] = atoms[base:base + 4]
-    return out[:rows]
+            for j in range(4):
+                out[r, 4 * g + j] = atoms[(blk * kg + g) * 512 + (rr % 32) * 16 + (rr // 32) * 4 + j]
+    return out
 
 
 def nvfp4_dequant(packed: np.ndarray, atoms: np.ndarray, tensor_scale: float, rows: int, k: int) -> np.ndarray:

@@ -100,9 +100,9 @@ def test_minimal_extents_exact(cuda_device, variant, mnk):
 @pytest.mark.parametrize("variant", ["tuned", "persistent_1cta"])
 @pytest.mark.parametrize("mnk", [(256, 256, 16384), (128, 64, 32768)])
 def test_long_k_exact(cuda_device, variant, mnk):
-    """Long reductions (256-512 k-blocks; the tuned variant splits the single
-    tile along K and exchanges partials): integer products stay exact in
-    FP32, so any dropped or doubled k-block shows."""
+    """Long reductions (256-512 k-blocks; the tuned variant cuts the single
+    tile's k-blocks over the clusters and fixes up the partials): integer
+    products stay exact in FP32, so any dropped or doubled k-block shows."""
     m, n, k = mnk
     a, b = inputs.reference_mode_operands(m, n, k)
     a, b = a[0], b[0]
@@ -238,13 +238,20 @@ def test_negative_iteration_count_rejected(cuda_device):
         plan.close()
 
 
+@pytest.mark.parametrize("snap", [None, "0"])
 @pytest.mark.parametrize("mnk", [(4096, 4096, 1024), (16384, 512, 1024), (512, 16384, 1024), (2304, 2048, 4096),
-                                 (640, 768, 2048), (32768, 512, 4096), (256, 2560, 3072)])
-def test_split_tail_exact(cuda_device, mnk, monkeypatch):
-    """Shapes whose last wave is partial run a split tail (tail tiles cut in
-    2 or 4 along K) in the tuned variant; BB_GEMM_STREAM_K=1 forces it even
-    for short K. Integer operands make every split of K exact."""
+                                 (640, 768, 2048), (32768, 512, 4096), (256, 2560, 3072), (512, 4096, 4096),
+                                 (1024, 4096, 4096), (2048, 4096, 4096), (1536, 4096, 1000)])
+def test_stream_k_exact(cuda_device, mnk, snap, monkeypatch):
+    """Shapes whose last wave is partial run a stream-K region (the tail's
+    (tile, k-block) iterations cut evenly over all clusters; partial pieces
+    fixed up by whichever finishes last) in the tuned variant;
+    BB_GEMM_STREAM_K=1 forces it even where the cost model declines, and
+    BB_GEMM_SK_SNAP=0 keeps range ends off the tile edges, so pieces of one
+    or two k-blocks occur. Integer operands make every split of K exact."""
     monkeypatch.setenv("BB_GEMM_STREAM_K", "1")
+    if snap is not None:
+        monkeypatch.setenv("BB_GEMM_SK_SNAP", snap)
     m, n, k = mnk
     a, b = inputs.reference_mode_operands(m, n, k)
     c = _run(a[0], b[0], torch.float32, "tuned", cuda_device)
@@ -252,9 +259,46 @@ def test_split_tail_exact(cuda_device, mnk, monkeypatch):
     assert torch.equal(c, ref)
 
 
-def test_split_tail_deterministic_bf16(cuda_device):
-    """The fix-up sums partials in a fixed order: repeated launches are
-    bit-identical even though arrival order varies."""
+@pytest.mark.parametrize("mnk", [(4096, 4096, 1024), (512, 4096, 4096), (1280, 1040, 520), (300, 600, 200),
+                                 (2304, 2056, 1024), (256, 264, 64)])
+def test_narrow_tail_exact(cuda_device, mnk, monkeypatch):
+    """The narrow tail: the partial last wave's 256-wide tiles computed as
+    two half-width (256 x 128) items on twice as many clusters, in the same
+    kernel as the whole tiles (BB_GEMM_NARROW=1 forces it where legal).
+    Ragged N leaves a second half partly or wholly outside C. Integer
+    operands: exact in FP32 and in BF16."""
+    monkeypatch.setenv("BB_GEMM_NARROW", "1")
+    monkeypatch.setenv("BB_GEMM_TILE_N", "256")
+    m, n, k = mnk
+    a, b = inputs.reference_mode_operands(m, n, k)
+    ref = oracle.gemm_reference_fp32(a[0], b[0])
+    for out in (torch.float32, torch.bfloat16):
+        c = _run(a[0], b[0], out, "tuned", cuda_device)
+        assert torch.isfinite(c.float()).all(), "unwritten (NaN) output elements"
+        assert torch.equal(c, ref.to(out))
+
+
+def test_narrow_tail_epilogue_and_repeat(cuda_device, monkeypatch):
+    """alpha / beta on the half-width items, and repeated launches."""
+    monkeypatch.setenv("BB_GEMM_NARROW", "1")
+    monkeypatch.setenv("BB_GEMM_TILE_N", "256")
+    m, n, k = 4096, 4096, 512
+    a, b = inputs.reference_mode_operands(m, n, k)
+    a, b = a[0], b[0]
+    csrc = torch.randint(-4, 5, (m, n), generator=torch.Generator().manual_seed(9)).float()
+    c = torch.full((m, n), float("nan"), dtype=torch.float32, device=cuda_device)
+    plan = GemmPlan(a.to(cuda_device), b.to(cuda_device), c, variant="tuned")
+    src = csrc.to(cuda_device)
+    plan.set_epilogue(0.5, -1.5, src)
+    plan.run(3)
+    plan.synchronize()
+    plan.close()
+    assert torch.equal(c.cpu(), 0.5 * oracle.gemm_reference_fp32(a, b) - 1.5 * csrc)
+
+
+def test_stream_k_deterministic_bf16(cuda_device):
+    """The fix-up sums partials in k order whoever finishes last: repeated
+    launches are bit-identical even though arrival order varies."""
     a, b = inputs.baseline_mode_operands(4096, 4096, 2048)
     ad, bd = a.to(cuda_device), b.to(cuda_device)
     c = torch.empty(4096, 4096, dtype=torch.bfloat16, device=cuda_device)
@@ -270,6 +314,31 @@ def test_split_tail_deterministic_bf16(cuda_device):
     assert oracle.rel_frobenius(c.cpu().float(), ref) <= BF16_TOL
 
 
+def test_stream_k_concurrent_plans(cuda_device):
+    """Two stream-K plans launched at the same time on two streams share the
+    SMs, so some clusters of each launch only start when the other launch's
+    clusters exit. No piece waits for another (the last to finish does the
+    fix-up), so both complete without a timeout and stay exact."""
+    shapes = [(512, 4096, 4096), (2048, 4096, 2048)]
+    runs = []
+    for m, n, k in shapes:
+        a, b = inputs.reference_mode_operands(m, n, k)
+        a, b = a[0], b[0]
+        c = torch.full((m, n), float("nan"), dtype=torch.float32, device=cuda_device)
+        s = torch.cuda.Stream(device=cuda_device)
+        with torch.cuda.stream(s):
+            plan = GemmPlan(a.to(cuda_device), b.to(cuda_device), c, variant="tuned")
+        runs.append((plan, c, oracle.gemm_reference_fp32(a, b), s))
+    torch.cuda.synchronize()
+    for _ in range(5):
+        for plan, _, _, _ in runs:
+            plan.run(2)
+    for plan, c, ref, _ in runs:
+        plan.synchronize()
+        assert torch.equal(c.cpu(), ref)
+        plan.close()
+
+
 @pytest.mark.parametrize("tile_n", ["256", "512"])
 @pytest.mark.parametrize("mnk,force_split", [((512, 1024, 512), False), ((300, 600, 200), False),
                                              ((1024, 1536, 4096), True), ((4096, 4096, 3072), True),
@@ -277,8 +346,8 @@ def test_split_tail_deterministic_bf16(cuda_device):
 def test_tuned_tile_shapes_exact(cuda_device, monkeypatch, tile_n, mnk, force_split):
     """Both CTA-pair tile shapes of the tuned variant (256 x 256 with a
     double-buffered accumulator, 256 x 512 with two N = 256 MMAs per K step),
-    including ragged N (half of the second MMA outside C) and the split
-    tail, are exact on integer operands."""
+    including ragged N (half of the second MMA outside C) and the stream-K
+    region, are exact on integer operands."""
     monkeypatch.setenv("BB_GEMM_TILE_N", tile_n)
     if force_split:
         monkeypatch.setenv("BB_GEMM_STREAM_K", "1")
@@ -295,7 +364,7 @@ def test_tuned_tile_shapes_exact(cuda_device, monkeypatch, tile_n, mnk, force_sp
 
 EPI_CASES = [(v, mnk, None) for v in ("tuned", "persistent_1cta", "persistent_2cta")
              for mnk in ((512, 768, 320), (300, 264, 200), (1024, 1024, 4096))]
-EPI_CASES += [("tuned", (4096, 4096, 4096), None),   # split tail
+EPI_CASES += [("tuned", (4096, 4096, 4096), None),   # stream-K region
               ("tuned", (1024, 1024, 4096), "512")]  # 512-wide tile, eight-warp epilogue
 
 
@@ -304,7 +373,7 @@ EPI_CASES += [("tuned", (4096, 4096, 4096), None),   # split tail
 @pytest.mark.parametrize("alpha,beta,inplace", [(0.5, 0.0, False), (1.5, -2.0, False), (1.0, 1.0, True)])
 def test_alpha_beta_epilogue(cuda_device, out_dtype, variant, mnk, tile_n, alpha, beta, inplace, monkeypatch):
     """C = alpha A B^T + beta Csrc on every store path (whole tiles, the
-    512-wide tile, the split tail), Csrc separate or C itself. Integer
+    512-wide tile, the stream-K fix-up), Csrc separate or C itself. Integer
     operands, FP32 output: exact; BF16 output: within BF16 rounding."""
     if tile_n:
         monkeypatch.setenv("BB_GEMM_TILE_N", tile_n)

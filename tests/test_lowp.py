@@ -55,6 +55,7 @@ def test_scale_atom_layout_round_trip():
         assert atoms[rb, kg, (rr % 32) * 16 + (rr // 32) * 4 + jj] == scales[r, j]
     back = olp.unpack_scale_atoms(atoms.numpy(), 300, 384)
     np.testing.assert_array_equal(back, scales.numpy())
+    np.testing.assert_array_equal(olp.unpack_scale_atoms_bytewise(atoms.numpy(), 300, 384), scales.numpy())
 
 
 def test_nvfp4_quantize_matches_oracle_dequant():
