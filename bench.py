@@ -1,22 +1,30 @@
 #!/usr/bin/env python3
-"""Headline benchmark: the sm_100a BF16 GEMM on config 0 (4096^3 per GPU).
+"""Headline benchmark: the sm_100a BF16 GEMM on config 0 (4096^3), row-sharded.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
 
-Workload (config 0): C = A * B^T with A (M x K) and B (N x K)
-BF16 from N(0,1) (torch.Generator seed 0), FP32 accumulation, BF16 C, M = N =
-K = 4096 per GPU. At N GPUs the global problem is (4096 N) x 4096 x 4096 with
-A and C row-sharded (rank r owns rows [4096 r, 4096 (r+1))) and B replicated:
-per-GPU work is fixed ("weak" scaling) and no collective runs on the data
-path. One step = one GEMM launch over the rank's shard.
+Workload (config 0, and config 3's multi-GPU mode): C = A * B^T with A
+(M x K) and B (N x K) BF16 from N(0,1) (torch.Generator seed 0), FP32
+accumulation, BF16 C, M = N = K = 4096 for the WHOLE job. At N GPUs rank r
+owns a contiguous block of A's and C's rows (sharding.row_shard, 128-row
+granules) and B is replicated: the global problem is fixed ("strong"
+scaling) and no collective runs on the data path. One step = one GEMM launch
+over the rank's shard; ``value`` is the job's aggregate TFLOP/s,
+2 M N K / (max over ranks of the per-step time).
+
+Also reported: cuBLASLt on the same per-rank shard; the same job with 4096
+rows per rank ("weak": global M = 4096 N); 8192^3 row-sharded the same way;
+the block-scaled GEMMs (config 4, one GPU).
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
 on the GEMM's stream; L2 is flushed (a 256 MiB write) before every step,
 outside the events. A barrier + synchronize bracket the timed region, and
-the per-step time is the max over ranks. ``e2e`` times the same step through
-the C ABI with host buffers (bb_gemm_run_host: H2D A-shard and B from pinned
-memory, GEMM, D2H C).
+the per-step time is the max over ranks. Correctness: the whole C (NCCL
+all-gather of the row blocks at N > 1, outside the timed region) against
+the FP32 oracle on the CPU. ``e2e`` times the same step through the C ABI
+with host buffers (bb_gemm_run_host: H2D of the rank's A block and B from
+pinned memory, GEMM, D2H of its C block).
 
 ``--impl reference`` times the reference's CPU implementation of the path,
 the FP32 matmul oracle of gemm_comparison.py:2698-2715 (torch on the host
@@ -36,15 +44,18 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-M_PER_RANK = 4096
+M_DIM = 4096  # global M of the headline job (config 0)
 N_DIM = 4096
 K_DIM = 4096
+ROW_GRANULE = 128
+METRIC = "bf16_gemm_tflops"
+WORKLOAD = "gemm_bf16_config0_4096x4096x4096_rowsharded"
 FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
 def parse_args(argv=None):
-    ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on config 0 (4096^3 per GPU)")
+    ap = argparse.ArgumentParser(description="BF16 GEMM TFLOP/s on config 0 (4096^3, row-sharded over the GPUs)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -53,6 +64,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-cublaslt", action="store_true", help="skip the cuBLASLt comparator leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-lowp", action="store_true", help="skip the block-scaled (config 4) section")
+    ap.add_argument("--no-extra", action="store_true", help="skip the weak-scaling and 8192^3 sections")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -190,7 +202,7 @@ def cpu_matmul_sample(target_s: float = 10.0, max_reps: int = 5000) -> dict:
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    a, b = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM)
+    a, b = inputs.baseline_mode_operands(M_DIM, N_DIM, K_DIM)
     rows = 512
     a_s = a[:rows]
     oracle.gemm_reference_fp32(a_s, b)  # warm-up
@@ -218,14 +230,14 @@ def run_reference(args, world, rank):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    a, b = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM)
+    a, b = inputs.baseline_mode_operands(M_DIM, N_DIM, K_DIM)
     # Size each step as a row sample of the 4096^3 workload so a step takes
     # about a second on this host.
     probe = a[:256]
     t0 = time.perf_counter()
     oracle.gemm_reference_fp32(probe, b)
     t_probe = max(time.perf_counter() - t0, 1e-4)
-    rows = int(min(M_PER_RANK, max(256, 256 * (1.0 / t_probe))))
+    rows = int(min(M_DIM, max(256, 256 * (1.0 / t_probe))))
     rows = max(256, rows // 256 * 256)
     a_s = a[:rows]
     for _ in range(args.warmup):
@@ -239,11 +251,11 @@ def run_reference(args, world, rank):
     value = 2.0 * rows * N_DIM * K_DIM / (ms / 1000.0) / 1e12
     sample = f"FP32 torch.matmul of A rows [0,{rows}) x B^T per step (4096x4096x4096 N(0,1) seed-0 workload)"
     line = {
-        "metric": "bf16_gemm_tflops_per_gpu", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "gemm_bf16_config0_4096x4096x4096", "rows_per_step": rows,
+        "config": {"workload": WORKLOAD, "rows_per_step": rows,
                    "path": "FP32 matmul oracle of gemm_comparison.py:2698-2715 on the host cores"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -346,175 +358,282 @@ def run_lowp(args, stream, flush, peak_bf16: float, peak_kind: str) -> dict:
     return out
 
 
+def _timed_steps(stream, flush, fn, steps):
+    """Per-step device times (ms): L2 flushed before every step, outside the
+    events recorded on the GEMM's stream."""
+    import torch
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in evs:
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+    stream.synchronize()
+    return [e0.elapsed_time(e1) for e0, e1 in evs]
+
+
+def _hot_ms(stream, fn_n, iters):
+    """Back-to-back launches without flushing (the reference's own timing
+    method, gemm_comparison.py:3048-3067), ms per launch."""
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    fn_n(iters)
+    e1.record(stream)
+    stream.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def _sharded_job(args, world, rank, dev, stream, flush, m, n, k, a_rows_fn, check, sampler=None):
+    """One row-sharded GEMM job: this rank's (rows, n, k) block of the global
+    (m, n, k) problem, timed per step (L2 flushed), max over ranks; with
+    cuBLASLt on the same block. `a_rows_fn(row0, rows)` gives this rank's A
+    block on the CPU. `check` is "gather" (the whole C, all-gathered, against
+    the FP32 oracle on rank 0) or "rows" (a strided row sample of every
+    rank's block against the oracle for those rows)."""
+    import torch
+
+    import oracle
+    from gb300_microbench_b200 import _native as nat
+    from gb300_microbench_b200.gemm import CublasLtPlan, GemmPlan
+    from gb300_microbench_b200.sharding import gather_rows, row_shard
+
+    shards = [row_shard(m, world, r, ROW_GRANULE) for r in range(world)]
+    me = shards[rank]
+    b_cpu = a_rows_fn.b
+    a_cpu = a_rows_fn(me.row0, me.rows)
+    b = b_cpu.to(dev)
+    a = a_cpu.to(dev) if me.rows else None
+    c = torch.empty(max(me.rows, 1), n, dtype=torch.bfloat16, device=dev)
+    plan = GemmPlan(a, b, c[: me.rows], variant=args.variant, stream=stream) if me.rows else None
+    flops_local = 2.0 * me.rows * n * k
+    res = {"m": m, "n": n, "k": k, "rows_per_rank": [s.rows for s in shards]}
+
+    # Correctness before timing.
+    if plan:
+        plan.run()
+        plan.synchronize()
+    err = 0.0
+    if check == "gather":
+        full = gather_rows(c[: me.rows], shards) if world > 1 else c[: me.rows]
+        if rank == 0:
+            ref = oracle.gemm_reference_fp32(a_rows_fn(0, m), b_cpu)
+            err = oracle.rel_frobenius(full.float().cpu(), ref)
+        del full
+        err_all = all_max(world, err)
+        res["check"] = {"rel_frobenius_full_c": err_all, "rows_checked": m,
+                        "how": "NCCL all-gather of the row blocks, then the FP32 oracle on the CPU" if world > 1
+                        else "the FP32 oracle on the CPU"}
+    else:
+        idx = torch.arange(0, me.rows, 61)
+        if me.rows:
+            ref = oracle.gemm_reference_fp32(a_cpu[idx], b_cpu)
+            err = oracle.rel_frobenius(c[idx.to(dev)].float().cpu(), ref)
+        err_all = all_max(world, err)
+        res["check"] = {"rel_frobenius_sampled_rows": err_all, "rows_checked": "every 61st row of each rank's block"}
+    if err_all > 1e-2:
+        raise SystemExit(f"bench: GEMM {m}x{n}x{k} result check failed (rel Frobenius {err_all:.3e} > 1e-2)")
+
+    noop = lambda *a_: None  # noqa: E731
+    run = plan.run if plan else noop
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    n_samples0 = len(sampler.samples) if sampler else 0
+    launches0 = nat.kernel_launches()
+    step_ms = _timed_steps(stream, flush, run, args.steps)
+    torch.cuda.synchronize()
+    res["launches_timed"] = nat.kernel_launches() - launches0
+    res["clock_samples_timed"] = (len(sampler.samples) - n_samples0) if sampler else 0
+    barrier(world)
+    ms_local = statistics.mean(step_ms)
+    ms = all_max(world, ms_local)
+    hot = all_max(world, _hot_ms(stream, run, max(args.steps, 100)) if plan else 0.0)
+    res.update({"value": 2.0 * m * n * k / (ms / 1000.0) / 1e12, "ms_per_step": ms,
+                "per_gpu": 2.0 * m * n * k / (ms / 1000.0) / 1e12 / world,
+                "hot_cache_tflops": 2.0 * m * n * k / (hot / 1000.0) / 1e12,
+                "plan": plan.info if plan else None, "ms_local": ms_local,
+                "achieved_local": flops_local / (ms_local / 1000.0) / 1e12 if plan else 0.0})
+    if not args.no_cublaslt:
+        if me.rows:
+            c2 = torch.empty_like(c[: me.rows])
+            cmp = CublasLtPlan(a, b, c2, autotune=False, stream=stream)
+            cmp.run(args.warmup)
+            cl_local = statistics.mean(_timed_steps(stream, flush, cmp.run, args.steps))
+            cl_hot_local = _hot_ms(stream, cmp.run, max(args.steps, 100))
+            algo = cmp.algo_index
+            cmp.close()
+            del c2
+        else:
+            cl_local, cl_hot_local, algo = 0.0, 0.0, None
+        cl = all_max(world, cl_local)
+        cl_hot = all_max(world, cl_hot_local)
+        res["cublaslt"] = {"tflops": 2.0 * m * n * k / (cl / 1000.0) / 1e12, "ms_per_step": cl,
+                           "hot_tflops": 2.0 * m * n * k / (cl_hot / 1000.0) / 1e12, "algo_index": algo,
+                           "ratio_ours_vs_cublaslt": cl / ms, "ratio_hot": cl_hot / hot,
+                           "shape_per_rank": f"{max(s.rows for s in shards)}x{n}x{k}"}
+    return res, plan, a_cpu, b_cpu
+
+
 def run_ours(args, world, rank, local):
     import torch
 
-    from gb300_microbench_b200 import _native as nat
     from gb300_microbench_b200 import inputs
-    from gb300_microbench_b200.gemm import CublasLtPlan, GemmPlan
+    from gb300_microbench_b200.gemm import GemmPlan
 
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(device=dev)
-
-    # Rank r's shard of the global (4096 * world) x 4096 problem: the A row
-    # block is drawn with a per-rank seed, B is the same on every rank.
-    a_cpu, b_cpu = inputs.baseline_mode_operands(M_PER_RANK, N_DIM, K_DIM, seed=0)
-    if rank > 0:
-        g = torch.Generator().manual_seed(1000 + rank)
-        a_cpu = torch.randn(M_PER_RANK, K_DIM, generator=g).to(torch.bfloat16)
-    a = a_cpu.to(dev)
-    b = b_cpu.to(dev)
-    c = torch.empty(M_PER_RANK, N_DIM, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    flops = 2.0 * M_PER_RANK * N_DIM * K_DIM
 
-    plan = GemmPlan(a, b, c, variant=args.variant, stream=stream)
+    # Config 0's operands: the global A (4096 x 4096) and B, seed 0; each
+    # rank takes its row block of A.
+    a_glob, b_glob = inputs.baseline_mode_operands(M_DIM, N_DIM, K_DIM, seed=0)
 
-    def timed_steps(fn, steps):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        for e0, e1 in evs:
-            with torch.cuda.stream(stream):
-                flush.zero_()
-            e0.record(stream)
-            fn()
-            e1.record(stream)
-        stream.synchronize()
-        return [e0.elapsed_time(e1) for e0, e1 in evs]
+    def a_rows(row0, rows):
+        return a_glob[row0: row0 + rows]
 
-    # Correctness gate before timing: the oracle on a row block of C.
-    plan.run()
-    plan.synchronize()
-    import oracle
-
-    ref = oracle.gemm_reference_fp32(a_cpu[:256], b_cpu)
-    err = oracle.rel_frobenius(c[:256].float().cpu(), ref)
-    if err > 1e-2:
-        raise SystemExit(f"bench: GEMM result check failed (rel Frobenius {err:.3e} > 1e-2)")
-
-    for _ in range(args.warmup):
-        plan.run()
-    plan.synchronize()
+    a_rows.b = b_glob
 
     sampler = ClockSampler(gpu_index_for(local if world > 1 else 0))
-    launches0 = nat.kernel_launches()
-    barrier(world)
-    torch.cuda.synchronize()
     sampler.start()
-    step_ms = timed_steps(plan.run, args.steps)
-    torch.cuda.synchronize()
-    samples_timed = len(sampler.samples)
-    launches = nat.kernel_launches() - launches0
-    barrier(world)
-
-    # Hot-cache back-to-back figure (the reference's own timing method,
-    # gemm_comparison.py:3048-3067), reported beside the flushed one. It runs
-    # the same kernel straight after the timed steps, and the clock sampler
-    # keeps running through it: a short timed region (few steps, slow NVML
-    # queries on a busy 8-GPU host) can otherwise yield a single sample.
-    hot_iters = max(args.steps, 200)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    plan.run(hot_iters)
-    e1.record(stream)
-    stream.synchronize()
+    head, plan, a_blk, _ = _sharded_job(args, world, rank, dev, stream, flush, M_DIM, N_DIM, K_DIM, a_rows, "gather",
+                                        sampler)
     clocks = sampler.stop()
-    clocks["samples_timed_region"] = samples_timed
-    clocks["window"] = "timed steps + the hot-cache repeat of the same kernel that follows them"
-    plan.synchronize()
-    ms_local = statistics.mean(step_ms)
-    ms = all_max(world, ms_local)
-    value = world * flops / (ms / 1000.0) / 1e12
-    hot_ms = all_max(world, e0.elapsed_time(e1) / hot_iters)
+    launches = head["launches_timed"]
+    clocks["samples_timed_region"] = head["clock_samples_timed"]
+    clocks["window"] = "the headline job: check launch, warm-up, timed steps, hot-cache repeat, cuBLASLt comparator"
+    ms = head["ms_per_step"]
+    flops = 2.0 * M_DIM * N_DIM * K_DIM
 
-    # cuBLASLt on the same operands, same timing.
-    cublas = None
-    if not args.no_cublaslt:
-        c2 = torch.empty_like(c)
-        cmp = CublasLtPlan(a, b, c2, autotune=False, stream=stream)
-        cmp.run(args.warmup)
-        cl_ms = all_max(world, statistics.mean(timed_steps(cmp.run, args.steps)))
-        e0.record(stream)
-        cmp.run(args.steps)
-        e1.record(stream)
-        stream.synchronize()
-        cl_hot = all_max(world, e0.elapsed_time(e1) / args.steps)
-        cublas = {"tflops": world * flops / (cl_ms / 1000.0) / 1e12, "ms_per_step": cl_ms,
-                  "hot_tflops": world * flops / (cl_hot / 1000.0) / 1e12, "algo_index": cmp.algo_index,
-                  "ratio_ours_vs_cublaslt": cl_ms / ms, "ratio_hot": cl_hot / hot_ms}
-        cmp.close()
-        del c2
-
-    # End to end through the C ABI with host buffers.
-    a_h = a_cpu.pin_memory()
-    b_h = b_cpu.pin_memory()
-    c_h = torch.empty(M_PER_RANK, N_DIM, dtype=torch.bfloat16).pin_memory()
-    a_d = torch.empty_like(a)
-    b_d = torch.empty_like(b)
-    c_d = torch.empty_like(c)
-    eplan = GemmPlan(a_d, b_d, c_d, variant=args.variant, stream=stream)
-    for _ in range(2):
-        eplan.run_host(a_h, b_h, c_h)
+    # End to end through the C ABI with host buffers: this rank's A block and
+    # B in, its C block out, every step.
+    me_rows = a_blk.shape[0]
+    e2e = None
+    if me_rows:
+        a_h = a_blk.contiguous().pin_memory()
+        b_h = b_glob.pin_memory()
+        c_h = torch.empty(me_rows, N_DIM, dtype=torch.bfloat16).pin_memory()
+        eplan = GemmPlan(torch.empty_like(a_h, device=dev), torch.empty_like(b_h, device=dev),
+                         torch.empty(me_rows, N_DIM, dtype=torch.bfloat16, device=dev), variant=args.variant,
+                         stream=stream)
+        for _ in range(2):
+            eplan.run_host(a_h, b_h, c_h)
     e2e_steps = max(3, min(args.steps, 10))
     barrier(world)
     t_e2e = []
     for _ in range(e2e_steps):
         t0 = time.perf_counter()
-        eplan.run_host(a_h, b_h, c_h)
+        if me_rows:
+            eplan.run_host(a_h, b_h, c_h)
         t_e2e.append(time.perf_counter() - t0)
     e2e_s = all_max(world, statistics.mean(t_e2e))
-    # The host path runs row chunks as separate GEMMs (their tiling may
-    # differ from the whole problem's), so it is checked against the oracle.
-    e2e_err = oracle.rel_frobenius(c_h[:256].float(), ref)
+    import oracle
+
+    e2e_err = 0.0
+    if me_rows:
+        # The host path runs row chunks as separate GEMMs (their tiling may
+        # differ from the whole block's), so it is checked against the oracle.
+        ref = oracle.gemm_reference_fp32(a_h[:256], b_glob)
+        e2e_err = oracle.rel_frobenius(c_h[:256].float(), ref)
+        eplan.close()
+    e2e_err = all_max(world, e2e_err)
     if e2e_err > 1e-2:
         raise SystemExit(f"bench: end-to-end result check failed (rel Frobenius {e2e_err:.3e} > 1e-2)")
-    h2d = a_h.numel() * 2 + b_h.numel() * 2
-    d2h = c_h.numel() * 2
-    eplan.close()
+    # Bytes per step, whole job: every rank copies its A block and all of B
+    # in and its C block out.
+    h2d = M_DIM * K_DIM * 2 + world * N_DIM * K_DIM * 2
+    d2h = M_DIM * N_DIM * 2
+    e2e = {"value": flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "ms_per_step": e2e_s * 1000.0,
+           "path": "bb_gemm_run_host per rank (pinned host A block and B -> device, GEMM, C block -> pinned host; "
+                   "B first, then A in row chunks whose GEMMs and C copies overlap the remaining transfers)",
+           "check_rel_frobenius_rows_0_256_each_rank": e2e_err}
+
+    # Secondary jobs: the same shard per rank at 4096 rows each (weak), and
+    # 8192^3 row-sharded (strong).
+    extra = {}
+    if not args.no_extra:
+        def a_weak(row0, rows):
+            # Global A of 4096 * world rows: block r drawn with seed 1000 + r
+            # (block 0 is config 0's A), so no rank builds the whole matrix.
+            blocks = []
+            for r in range(row0 // 4096, (row0 + rows + 4095) // 4096):
+                if r == 0:
+                    blocks.append(a_glob)
+                else:
+                    g = torch.Generator().manual_seed(1000 + r)
+                    blocks.append(torch.randn(4096, K_DIM, generator=g).to(torch.bfloat16))
+            full = torch.cat(blocks) if blocks else a_glob[:0]
+            off = row0 - (row0 // 4096) * 4096
+            return full[off: off + rows]
+
+        a_weak.b = b_glob
+        weak, wplan, _, _ = _sharded_job(args, world, rank, dev, stream, flush, 4096 * world, N_DIM, K_DIM, a_weak,
+                                         "rows")
+        if wplan:
+            wplan.close()
+        extra["weak_4096_rows_per_rank"] = weak
+        a8, b8 = inputs.baseline_mode_operands(8192, 8192, 8192, seed=0)
+
+        def a8_rows(row0, rows):
+            return a8[row0: row0 + rows]
+
+        a8_rows.b = b8
+        big, bplan, _, _ = _sharded_job(args, world, rank, dev, stream, flush, 8192, 8192, 8192, a8_rows, "rows")
+        if bplan:
+            bplan.close()
+        extra["strong_8192x8192x8192"] = big
+        del a8, b8
 
     pk, pk_kind = peaks()
     peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    achieved = flops / (ms_local / 1000.0) / 1e12
-    traffic = committed_traffic()
+    achieved = all_max(world, head["achieved_local"]) if world > 1 else head["achieved_local"]
+    traffic = committed_traffic() if world == 1 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_matmul_sample()
 
-    # Config 4 (block-scaled FP8 / NVFP4), single-GPU runs only.
     lowp_res = None
     if world == 1 and not args.no_lowp:
-        del a_h, b_h, c_h, a_d, b_d, c_d
         lowp_res = run_lowp(args, stream, flush, peak, pk_kind)
 
     if rank == 0:
+        rows_max = max(head["rows_per_rank"])
         line = {
-            "metric": "bf16_gemm_tflops_per_gpu", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "metric": METRIC, "value": head["value"], "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "gemm_bf16_config0_4096x4096x4096", "m_per_rank": M_PER_RANK, "n": N_DIM,
-                       "k": K_DIM, "global_m": M_PER_RANK * world, "variant": args.variant,
-                       "c_dtype": "bf16", "inputs": "N(0,1) BF16, torch.Generator seed 0 (rank>0: seed 1000+rank)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "value_per_gpu": head["per_gpu"],
+            "config": {"workload": WORKLOAD, "m": M_DIM, "n": N_DIM, "k": K_DIM,
+                       "rows_per_rank": head["rows_per_rank"], "variant": args.variant, "c_dtype": "bf16",
+                       "inputs": "N(0,1) BF16, torch.Generator seed 0 (global A and B; rank r takes its row block)",
                        "l2": "flushed before every step (256 MiB write, outside the events)",
-                       "parallelism": f"rowshard{world}", "plan": plan.info},
-            "hot_cache_tflops": world * flops / (hot_ms / 1000.0) / 1e12,
-            "cublaslt": cublas,
+                       "parallelism": f"rowshard{world} (A and C row blocks, B replicated, no collective when timed)",
+                       "plan": head["plan"]},
+            "hot_cache_tflops": head["hot_cache_tflops"],
+            "cublaslt": head.get("cublaslt"),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
+                         "per": f"one launch over a {rows_max}x{N_DIM}x{K_DIM} shard (the slowest rank)",
                          "peak_source": f"{pk_kind} bf16_tflops (burst cuBLAS bf16 8192^3)"},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * flops / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1000.0,
-                    "path": "bb_gemm_run_host (pinned host A, B -> device, GEMM, C -> pinned host; B first, then A "
-                            "in row chunks whose GEMMs and C copies overlap the remaining transfers)",
-                    "check_rel_frobenius_rows_0_256": e2e_err},
+            "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
-            "check": {"rel_frobenius_rows_0_256": err},
+            "check": head["check"],
+            "extra": extra,
             "lowp_config4": lowp_res,
         }
         print(json.dumps(line), flush=True)
-    plan.close()
+    if plan:
+        plan.close()
     return 0
 
 
