@@ -1,0 +1,191 @@
+#!/usr/bin/env python3
+"""The reference's own GEMM kernels (the pinned upstream CuTe DSL examples)
+beside this build's kernel and cuBLASLt, on the same B200 (one GPU).
+
+    python baseline/run_reference_gemm.py [--iterations N] [--warmup-iterations N] [--out results/...csv]
+
+The reference's gemm_comparison.py builds three candidates from the pinned
+CUTLASS examples ``blackwell/dense_gemm.py`` (DenseGemmKernel) and
+``blackwell/dense_gemm_persistent.py`` (PersistentDenseGemmKernel) in the
+slots of gemm_comparison.py:209-245 (tile, cluster, 2-CTA instructions), with
+FP32 accumulation, TMA store, A and B K-major BF16 and C N-major FP32
+(:137-145), compiles each with ``cute.compile`` (:2806-2906) and times N
+back-to-back launches between two CUDA events after a correctness-checked
+first launch and warm-up (:2908-2950, :3048-3067), on the operands the
+example's own ``create_tensors`` draws under seed 1111 (:2625-2690). This
+script does exactly that, importing the example files by path from the
+CUTLASS tree installed in this image (byte-identical to the pinned ones),
+then runs this build's four variants and cuBLASLt on the same operand values
+the same way, and writes one CSV row per (shape, implementation).
+
+The checks are the reference's: every element |c - ref| <= 0.1 + 1e-5 |ref|
+against an IEEE-FP32 matmul of the operands (gemm_comparison.py:2698-2755);
+the integer operands make the products exact, so every candidate must agree
+with it bit for bit in practice.
+
+One GPU only. The upstream examples may issue cluster-wide TMA loads in
+some configurations; the three slots run here use one-CTA or CTA-pair
+clusters whose operand loads are per CTA, all on this GPU's own memory.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import importlib.util
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+SHAPES = ((4096, 4096, 4096, 1), (8192, 8192, 8192, 1), (16384, 512, 4096, 1), (32768, 512, 4096, 1),
+          (512, 16384, 4096, 1))
+SLOTS = (
+    ("nonpersistent_1cta", "DenseGemmKernel", (128, 128), (1, 1), False, False),
+    ("persistent_1cta", "PersistentDenseGemmKernel", (128, 128), (1, 1), False, True),
+    ("persistent_2cta", "PersistentDenseGemmKernel", (256, 128), (2, 1), True, True),
+)
+
+
+def example_dir() -> Path:
+    import flashinfer
+
+    return Path(flashinfer.__file__).resolve().parent / "data/cutlass/examples/python/CuTeDSL/blackwell"
+
+
+def load_module(path: Path, name: str):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def hot_ms(torch, stream, launch, iterations):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iterations):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iterations
+
+
+def check(torch, c, ref):
+    diff = (c - ref).abs()
+    bad = int((diff > 0.1 + 1e-5 * ref.abs()).sum().item()) + int((~torch.isfinite(c)).sum().item())
+    return bad, float(diff.max().item())
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--iterations", type=int, default=20)
+    ap.add_argument("--warmup-iterations", type=int, default=5)
+    ap.add_argument("--out", default=str(ROOT / "results" / "reference_on_b200_gemm.csv"))
+    args = ap.parse_args(argv)
+
+    import cuda.bindings.driver as cuda
+    import cutlass
+    import cutlass.cute as cute
+    import cutlass.utils as utils
+    import torch
+
+    from gb300_microbench_b200.gemm import VARIANTS, CublasLtPlan, GemmPlan
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    d = example_dir()
+    modules = {False: load_module(d / "dense_gemm.py", "upstream_dense_gemm"),
+               True: load_module(d / "dense_gemm_persistent.py", "upstream_dense_gemm_persistent")}
+    torch_stream = torch.cuda.current_stream()
+    cute_stream = cuda.CUstream(torch_stream.cuda_stream)
+    rows = []
+    compiled = {}
+    for (m, n, k, l) in SHAPES:
+        flops = 2.0 * m * n * k * l
+        (a_t, b_t, c_t, a_cpu, b_cpu, _c_cpu, c_gpu) = modules[False].create_tensors(
+            l, m, n, k, "k", "k", "n", cutlass.BFloat16, cutlass.Float32)
+        ref = torch.einsum("mkl,nkl->mnl", a_cpu.float().cuda(), b_cpu.float().cuda())
+        shape = f"{m}x{n}x{k}x{l}"
+
+        for variant, cls_name, tiler, cluster, two_cta, persistent in SLOTS:
+            gemm = getattr(modules[persistent], cls_name)(cutlass.Float32, two_cta, tiler, cluster, True)
+            if persistent:
+                ok = gemm.can_implement((m, n, k, l), a_t.element_type, b_t.element_type, c_t.element_type,
+                                        "k", "k", "n")
+            else:
+                ok = gemm.can_implement(a_t, b_t, c_t)
+            if not ok:
+                rows.append({"shape": shape, "impl": "cutedsl", "variant": variant, "note": "can_implement false"})
+                continue
+            extra = ()
+            if persistent:
+                extra = (utils.HardwareInfo().get_max_active_clusters(cluster[0] * cluster[1]),)
+            key = variant
+            t0 = time.perf_counter()
+            if key not in compiled:
+                # The tensors carry dynamic layouts, so one compile serves every shape.
+                compiled[key] = cute.compile(gemm, a_t, b_t, c_t, *extra, cute_stream)
+            compile_s = time.perf_counter() - t0
+            fn = compiled[key]
+            c_gpu.fill_(float("nan"))
+            fn(a_t, b_t, c_t, cute_stream)
+            torch.cuda.synchronize()
+            bad, max_abs = check(torch, c_gpu, ref)
+            for _ in range(args.warmup_iterations):
+                fn(a_t, b_t, c_t, cute_stream)
+            torch.cuda.synchronize()
+            ms = hot_ms(torch, torch_stream, lambda: fn(a_t, b_t, c_t, cute_stream), args.iterations)
+            rows.append({"shape": shape, "impl": "cutedsl", "variant": variant, "tflops": f"{flops / ms / 1e9:.1f}",
+                         "kernel_time_ms": f"{ms:.6f}", "correctness": "PASS" if bad == 0 else "FAIL",
+                         "max_abs_error": max_abs, "compile_s": f"{compile_s:.1f}", "note": ""})
+            print(f"{shape} cutedsl {variant}: {flops / ms / 1e9:.1f} TFLOP/s bad={bad}", file=sys.stderr)
+
+        # This build's kernels and cuBLASLt on the same operand values.
+        a2 = a_cpu.permute(2, 0, 1).contiguous().cuda()  # (L, M, K)
+        b2 = b_cpu.permute(2, 0, 1).contiguous().cuda()  # (L, N, K)
+        ref2 = ref.permute(2, 0, 1)
+        for variant in VARIANTS:
+            c2 = torch.full((l, m, n), float("nan"), dtype=torch.float32, device="cuda")
+            plan = GemmPlan(a2, b2, c2, variant=variant)
+            plan.run()
+            plan.synchronize()
+            bad, max_abs = check(torch, c2, ref2)
+            plan.run(args.warmup_iterations)
+            plan.synchronize()
+            ms = hot_ms(torch, plan.stream, lambda: plan.run(), args.iterations)
+            rows.append({"shape": shape, "impl": "ours", "variant": variant, "tflops": f"{flops / ms / 1e9:.1f}",
+                         "kernel_time_ms": f"{ms:.6f}", "correctness": "PASS" if bad == 0 else "FAIL",
+                         "max_abs_error": max_abs, "compile_s": "", "note": f"tile {plan.info['mma_tiler_m']}x"
+                                                                             f"{plan.info['mma_tiler_n']}"})
+            print(f"{shape} ours {variant}: {flops / ms / 1e9:.1f} TFLOP/s bad={bad}", file=sys.stderr)
+            plan.close()
+            del c2
+        c3 = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+        cmp = CublasLtPlan(a2[0], b2[0], c3, layout="reference")
+        cmp.run()
+        torch.cuda.synchronize()
+        bad, max_abs = check(torch, c3, ref2[0])
+        cmp.run(args.warmup_iterations)
+        ms = hot_ms(torch, cmp.stream, lambda: cmp.run(), args.iterations)
+        rows.append({"shape": shape, "impl": "cublaslt", "variant": "cublaslt", "tflops": f"{flops / ms / 1e9:.1f}",
+                     "kernel_time_ms": f"{ms:.6f}", "correctness": "PASS" if bad == 0 else "FAIL",
+                     "max_abs_error": max_abs, "compile_s": "", "note": f"algo {cmp.algo_index}"})
+        print(f"{shape} cublaslt: {flops / ms / 1e9:.1f} TFLOP/s bad={bad}", file=sys.stderr)
+        cmp.close()
+        del a_t, b_t, c_t, c_gpu, a2, b2, c3, ref, ref2
+
+    out = Path(args.out)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    fields = ["shape", "impl", "variant", "tflops", "kernel_time_ms", "correctness", "max_abs_error", "compile_s",
+              "note"]
+    with out.open("w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=fields, lineterminator="\n")
+        w.writeheader()
+        for r in rows:
+            w.writerow({f: r.get(f, "") for f in fields})
+    print(f"wrote {out}", file=sys.stderr)
+    return 0 if all(r.get("correctness", "PASS") == "PASS" for r in rows) else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -175,8 +175,10 @@ def _xor_of(sink_list) -> int:
 
 
 def run_config(method: str, cfg: dict, gpu: cm.GpuInfo, uuid: str, print_header: bool = True,
-               out=sys.stdout) -> int:
+               out=None) -> int:
     import torch
+
+    out = out if out is not None else sys.stdout  # resolved per call (callers may redirect stdout)
 
     from .. import streaming
 

@@ -156,8 +156,10 @@ def format_row(method, cfg, sample, cycles, max_abs, gpu, commit, dirty) -> str:
     return ",".join(fields)
 
 
-def run_config(method: str, cfg: dict, gpu: cm.GpuInfo, print_header: bool = True, out=sys.stdout) -> int:
+def run_config(method: str, cfg: dict, gpu: cm.GpuInfo, print_header: bool = True, out=None) -> int:
     import torch
+
+    out = out if out is not None else sys.stdout  # resolved per call (callers may redirect stdout)
 
     from .. import umma
 

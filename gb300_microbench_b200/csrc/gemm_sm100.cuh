@@ -37,6 +37,7 @@ struct Plan {
   int* status = nullptr;  // device word: 0, or the code of a timed-out wait
   // Epilogue D = alpha * acc + beta * c_src (bb_gemm_plan_set_epilogue).
   int epi_mode = 0;
+  int spin = 0;  // ring waits that spin (bit 0 producer, bit 1 MMA warp)
   float alpha = 1.0f, beta = 0.0f;
   const void* c_src = nullptr;
   int64_t launches = 0;
