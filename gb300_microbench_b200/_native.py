@@ -129,6 +129,8 @@ BENCH_SIGNATURES: dict[str, tuple] = {
     "bb_fill_uniform_u32": (c_int, [c_void_p, c_int64, c_uint64, c_void_p]),
     "bb_umma_run": (c_int, [c_int, c_int, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_void_p]),
+    "bb_umma_run_ex": (c_int, [c_int, c_int, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_void_p]),
     "bb_umma_kernel_name": (c_char_p, [c_int, c_int, c_int]),
     "bb_test_wait_timeout": (c_int, [c_int64, c_void_p, c_void_p]),
     "bb_kernel_launches": (c_int64, []),

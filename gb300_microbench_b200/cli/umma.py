@@ -5,14 +5,17 @@ sm_100a probes of libb200bench.so.
     python -m gb300_microbench_b200.cli.umma {umma_1sm,umma_2sm} --self-test
     python -m gb300_microbench_b200.cli.umma {umma_1sm,umma_2sm} --run-kind {smoke,benchmark}
         --n {64,128,256} --depth {4,16,32,64,128,256} --iterations N --warmup-iterations N
-        --repetitions N [--operands {pattern,random}] [--seed N]
+        --repetitions N [--operands {pattern,random}] [--seed N] [--handshake {cluster,none}]
 
 Flags, exit codes and the 37-column CSV are the reference's
 (umma_1sm.cu:965-995); depths 32 and 128 (the baseline-mode grid) and N(0,1)
 operands (``--operands random``, checked against an FP32 host
 restatement of depth * A * B^T within 1e-5 relative Frobenius error) are
 additions. Pattern operands are checked for exact equality, every
-repetition, as the reference does.
+repetition, as the reference does. ``umma_2sm`` runs the reference's loop:
+a per-iteration handshake of both CTAs (each waits on its own mbarrier,
+then a cluster barrier) inside the timed region (umma_2sm.cu:617-659);
+``--handshake none`` (an addition) times only the issuing CTA's waits.
 """
 from __future__ import annotations
 
@@ -45,11 +48,12 @@ Usage:
   {method} --self-test
   {method} --run-kind {{smoke,benchmark}} --n {{64,128,256}} --depth {{4,16,32,64,128,256}} \\
            --iterations N --warmup-iterations N --repetitions N [--operands {{pattern,random}}] [--seed N]
+           [--handshake {{cluster,none}}]   (umma_2sm: per-iteration CTA-pair handshake, default cluster)
 """
 
 
 def parse(argv: list[str]) -> dict:
-    cfg = {"help": False, "self_test": False, "operands": "pattern", "seed": 0}
+    cfg = {"help": False, "self_test": False, "operands": "pattern", "seed": 0, "handshake": "cluster"}
     seen = set()
     i = 0
     while i < len(argv):
@@ -96,6 +100,11 @@ def parse(argv: list[str]) -> dict:
         elif a == "--seed":
             v, i = cm.take_value(argv, i, a)
             cfg["seed"] = cm.parse_int(v, 0, (1 << 63) - 1, a)
+        elif a == "--handshake":
+            v, i = cm.take_value(argv, i, a)
+            if v not in ("cluster", "none"):
+                raise cm.UsageError("--handshake must be 'cluster' or 'none'")
+            cfg["handshake"] = v
         else:
             raise cm.UsageError(f"unknown argument: {a}")
     if cfg["help"]:
@@ -166,7 +175,8 @@ def run_config(method: str, cfg: dict, gpu: cm.GpuInfo, print_header: bool = Tru
     cg = METHODS[method]
     a, b = operands_for(cg, cfg["n"], cfg["operands"], cfg["seed"])
     want = expected_d(a, b, cfg["depth"])
-    probe = umma.UmmaProbe(cg, cfg["n"], cfg["depth"], a.cuda(), b.cuda())
+    probe = umma.UmmaProbe(cg, cfg["n"], cfg["depth"], a.cuda(), b.cuda(),
+                           handshake=cg == 2 and cfg.get("handshake", "cluster") == "cluster")
 
     def once(timed: bool):
         probe.launch(cfg["iterations"], timed=timed)
@@ -201,7 +211,7 @@ def self_test(method: str) -> int:
     for n in N_VALUES:
         for depth in DEPTHS:
             a, b = operands_for(cg, n, "pattern", 0)
-            probe = umma.UmmaProbe(cg, n, depth, a.cuda(), b.cuda())
+            probe = umma.UmmaProbe(cg, n, depth, a.cuda(), b.cuda(), handshake=cg == 2)
             probe.launch(SELF_TEST_ITERATIONS, timed=False)
             d, _ = probe.result()
             ok, mism, max_abs = check_d(d, expected_d(a, b, depth), "pattern")

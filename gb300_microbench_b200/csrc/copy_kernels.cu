@@ -28,6 +28,8 @@
 
 #include <atomic>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -39,6 +41,7 @@ namespace copy {
 constexpr int kLdgstsThreads = 128;
 constexpr int kTmaConsumerThreads = 128;
 constexpr int kTmaThreads = kTmaConsumerThreads + 32;
+constexpr int kTmaMaxVecPerThread = 32768 / 16 / kTmaConsumerThreads;  // stages of at most 32 KiB
 constexpr uint64_t kPatternSalt = 0xD1B54A32D192ED03ull;
 
 // SplitMix64 finaliser (the pattern generator of ldgsts.cu:220-232).
@@ -86,7 +89,7 @@ __device__ __forceinline__ uint32_t cta_xor(uint32_t v, uint32_t* scratch) {
 template <int STAGES, int COPIES, bool VALIDATE>
 __device__ __forceinline__ void ldgsts_body(const uint4* __restrict__ src, int64_t total_vec, int64_t total_tiles,
                                             int64_t passes, int64_t rotation, uint32_t* __restrict__ sink,
-                                            unsigned long long* __restrict__ mismatches) {
+                                            unsigned long long* __restrict__ mismatches, int pipe) {
   constexpr int kVecPerTile = kLdgstsThreads * COPIES;
   constexpr int kStageBytes = kVecPerTile * 16;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -96,6 +99,7 @@ __device__ __forceinline__ void ldgsts_body(const uint4* __restrict__ src, int64
   cta_range(total_tiles, t0, n);
   uint32_t total = 0;
   unsigned long long bad = 0;
+  const uint32_t zmask = static_cast<uint32_t>(total_vec >> 62);  // 0 for every real buffer
   if (n > 0) {
     for (int64_t p = 0; p < passes; ++p) {
       const int64_t rot = (rotation + p) % n;
@@ -111,9 +115,21 @@ __device__ __forceinline__ void ldgsts_body(const uint4* __restrict__ src, int64
 #pragma unroll
         for (int c = 0; c < COPIES; ++c) {
           const int v = tid + c * kLdgstsThreads;
-          if (vbase + v < total_vec) cp_async_16(slot + v * 16, src + vbase + v);
+          if (vbase + v < total_vec) {
+            cp_async_16(slot + v * 16, src + vbase + v);
+          }
         }
       };
+      // Consumes tile s and refills its slot with tile s + STAGES: this
+      // thread's vectors of the slot are loaded into registers first, then
+      // the whole refill is issued at once (one burst per stage, as the
+      // stage issue itself), and only then are the values XORed, so STAGES
+      // tiles stay in flight while a tile is reduced (never more: the slot
+      // is refilled only after it was read). Each thread reads and rewrites
+      // only the positions it copied itself; the refill's shared addresses
+      // carry a data dependence on the values read (AND with a zero the
+      // compiler cannot see), so no refill can issue before its reads
+      // returned.
       auto consume = [&](int64_t s) {
         const int64_t vbase = tile_of(s) * kVecPerTile;
         const uint4* slot = reinterpret_cast<const uint4*>(smem + (s % STAGES) * kStageBytes);
@@ -133,12 +149,67 @@ __device__ __forceinline__ void ldgsts_body(const uint4* __restrict__ src, int64
           }
         }
       };
-      for (int64_t s = 0; s < n + STAGES - 1; ++s) {
-        if (s < n) issue(s);
-        cp_async_commit();  // possibly empty: keeps the group count uniform
-        if (s >= STAGES - 1) {
+      auto consume_refill = [&](int64_t s) {
+        const int64_t vbase = tile_of(s) * kVecPerTile;
+        const bool refill = s + STAGES < n;
+        const int64_t nbase = refill ? tile_of(s + STAGES) * kVecPerTile : 0;
+        const uint32_t slot_u32 = smem_u32(smem + (s % STAGES) * kStageBytes);
+        const uint4* slot = reinterpret_cast<const uint4*>(smem + (s % STAGES) * kStageBytes);
+        uint4 x[COPIES];
+        uint32_t dep = 0;
+#pragma unroll
+        for (int c = 0; c < COPIES; ++c) {
+          const int v = tid + c * kLdgstsThreads;
+          x[c] = (vbase + v < total_vec) ? slot[v] : make_uint4(0, 0, 0, 0);
+          dep |= x[c].x;
+        }
+        dep &= zmask;
+        if (refill) {
+#pragma unroll
+          for (int c = 0; c < COPIES; ++c) {
+            const int v = tid + c * kLdgstsThreads;
+            if (nbase + v < total_vec) {
+              cp_async_16(slot_u32 + v * 16 + dep, src + nbase + v);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < COPIES; ++c) {
+          const int v = tid + c * kLdgstsThreads;
+          if (vbase + v < total_vec) {
+            acc.x ^= x[c].x;
+            acc.y ^= x[c].y;
+            acc.z ^= x[c].z;
+            acc.w ^= x[c].w;
+            if constexpr (VALIDATE) {
+              const uint4 e = pattern_vector(static_cast<uint64_t>(vbase + v));
+              bad += (x[c].x != e.x || x[c].y != e.y || x[c].z != e.z || x[c].w != e.w) ? 1 : 0;
+            }
+          }
+        }
+      };
+      if (pipe & 1) {
+        // Refill form: STAGES tiles in flight while one is reduced.
+        for (int64_t s = 0; s < STAGES; ++s) {
+          if (s < n) issue(s);
+          cp_async_commit();  // possibly empty: keeps the group count uniform
+        }
+        for (int64_t s = 0; s < n; ++s) {
           cp_async_wait<STAGES - 1>();
-          consume(s - (STAGES - 1));
+          consume_refill(s);
+          cp_async_commit();
+        }
+      } else {
+        // Classic form (the reference's order): tile s is issued into the
+        // slot freed by the previous reduction, then tile s - STAGES + 1 is
+        // waited for and reduced in place.
+        for (int64_t s = 0; s < n + STAGES - 1; ++s) {
+          if (s < n) issue(s);
+          cp_async_commit();  // possibly empty: keeps the group count uniform
+          if (s >= STAGES - 1) {
+            cp_async_wait<STAGES - 1>();
+            consume(s - (STAGES - 1));
+          }
         }
       }
       cp_async_wait<0>();
@@ -157,15 +228,15 @@ __device__ __forceinline__ void ldgsts_body(const uint4* __restrict__ src, int64
 template <int STAGES, int COPIES>
 __global__ void __launch_bounds__(kLdgstsThreads, 1)
     ldgsts_benchmark_kernel(const uint4* __restrict__ src, int64_t total_vec, int64_t total_tiles, int64_t passes,
-                            int64_t rotation, uint32_t* __restrict__ sink) {
-  ldgsts_body<STAGES, COPIES, false>(src, total_vec, total_tiles, passes, rotation, sink, nullptr);
+                            int64_t rotation, uint32_t* __restrict__ sink, int pipe) {
+  ldgsts_body<STAGES, COPIES, false>(src, total_vec, total_tiles, passes, rotation, sink, nullptr, pipe);
 }
 
 template <int STAGES, int COPIES>
 __global__ void __launch_bounds__(kLdgstsThreads, 1)
     ldgsts_validate_kernel(const uint4* __restrict__ src, int64_t total_vec, int64_t total_tiles,
                            uint32_t* __restrict__ sink, unsigned long long* __restrict__ mismatches) {
-  ldgsts_body<STAGES, COPIES, true>(src, total_vec, total_tiles, 1, 0, sink, mismatches);
+  ldgsts_body<STAGES, COPIES, true>(src, total_vec, total_tiles, 1, 0, sink, mismatches, 1);
 }
 
 // ------------------------------------------------------------------ TMA
@@ -192,6 +263,7 @@ __device__ __forceinline__ void tma_body(const CUtensorMap* tmap, int64_t total_
   int64_t t0, n;
   cta_range(total_tiles, t0, n);
   const int vec_per_tile = stage_bytes / 16;
+  const uint32_t zmask = static_cast<uint32_t>(total_vec >> 62);  // 0 for every real buffer
   uint32_t total = 0;
   unsigned long long bad = 0;
 
@@ -239,21 +311,36 @@ __device__ __forceinline__ void tma_body(const CUtensorMap* tmap, int64_t total_
         if (i >= n) i -= n;
         const int64_t vbase = (t0 + i) * vec_per_tile;
         const uint4* slot = reinterpret_cast<const uint4*>(smem + stage * stage_bytes);
-        for (int v = tid; v < vec_per_tile; v += kTmaConsumerThreads) {
-          if (vbase + v < total_vec) {
-            const uint4 x = slot[v];
-            acc.x ^= x.x;
-            acc.y ^= x.y;
-            acc.z ^= x.z;
-            acc.w ^= x.w;
-            if constexpr (VALIDATE) {
+        // This thread's vectors (at most kTmaMaxVecPerThread) into registers;
+        // the slot is released as soon as they have arrived (the OR below
+        // waits for every load), and the XOR runs after the release.
+        uint4 x[kTmaMaxVecPerThread];
+        uint32_t arrived = 0;
+#pragma unroll
+        for (int c = 0; c < kTmaMaxVecPerThread; ++c) {
+          const int v = tid + c * kTmaConsumerThreads;
+          x[c] = (v < vec_per_tile && vbase + v < total_vec) ? slot[v] : make_uint4(0, 0, 0, 0);
+          arrived |= x[c].x;
+        }
+        // The mask carries a data dependence on every loaded value (OR-ed,
+        // then AND-ed with a zero the compiler cannot see), so the warp
+        // barrier, and the release after it, wait for all of the loads.
+        __syncwarp(0xffffffffu | (arrived & zmask));
+        if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
+#pragma unroll
+        for (int c = 0; c < kTmaMaxVecPerThread; ++c) {
+          const int v = tid + c * kTmaConsumerThreads;
+          acc.x ^= x[c].x;
+          acc.y ^= x[c].y;
+          acc.z ^= x[c].z;
+          acc.w ^= x[c].w;
+          if constexpr (VALIDATE) {
+            if (v < vec_per_tile && vbase + v < total_vec) {
               const uint4 e = pattern_vector(static_cast<uint64_t>(vbase + v));
-              bad += (x.x != e.x || x.y != e.y || x.z != e.z || x.w != e.w) ? 1 : 0;
+              bad += (x[c].x != e.x || x[c].y != e.y || x[c].z != e.z || x[c].w != e.w) ? 1 : 0;
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -402,6 +489,16 @@ static int set_smem(K kern, int smem) {
 #define BB_LDGSTS_CASES(X) \
   X(2, 4) X(2, 8) X(2, 16) X(3, 2) X(3, 5) X(3, 10) X(4, 2) X(4, 4) X(4, 8) X(8, 1) X(8, 2) X(8, 4)
 
+// LDGSTS pipeline form: the refill form (1) keeps every stage in flight
+// while one is reduced and wins where stages are small (2-4 KiB: 8 x 16 KiB
+// 2112 -> 3173 GB/s, 4 x 16 KiB 3449 -> 3536 on one box); with larger
+// stages the classic form (0) streams faster (4 x 64 KiB 6990 against 5191).
+// BB_COPY_PIPE=0|1 overrides.
+static int ldgsts_pipe(const Geometry& g) {
+  if (const char* e = std::getenv("BB_COPY_PIPE")) return std::atoi(e) != 0 ? 1 : 0;
+  return g.stage_bytes <= 4096 ? 1 : 0;
+}
+
 static int launch_ldgsts(const Geometry& g, bool validate, const void* src, int64_t bytes, int64_t passes,
                          int64_t rotation, uint32_t* sink, unsigned long long* mism, cudaStream_t st) {
   const int64_t nvec = bytes / 16;
@@ -416,7 +513,7 @@ static int launch_ldgsts(const Geometry& g, bool validate, const void* src, int6
       int rc = set_smem(ldgsts_benchmark_kernel<S, C>, g.smem);                                         \
       if (rc != BB_OK) return rc;                                                                       \
       ldgsts_benchmark_kernel<S, C><<<g.grid, kLdgstsThreads, g.smem, st>>>(s, nvec, g.total_tiles, passes, \
-                                                                            rotation, sink);            \
+                                                                            rotation, sink, ldgsts_pipe(g)); \
     }                                                                                                   \
     return check_cuda(cudaGetLastError(), "ldgsts launch");                                             \
   }

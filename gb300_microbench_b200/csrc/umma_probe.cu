@@ -11,12 +11,14 @@
 // enable_input_d = 0), commits to its own mbarrier and waits for it (bounded)
 // before the next iteration; %clock64 brackets the loop.
 //
-// 2-SM difference from the reference: the reference signals each
-// iteration's commit to both CTAs and runs a cluster barrier every iteration
-// so the peer observes every phase (umma_2sm.cu:617-659). Here only the
-// issuing CTA waits per iteration; the peer learns of the final MMA through
-// one extra commit to its own mbarrier after the loop, so the timed loop
-// contains no cluster handshake.
+// 2-SM probes have two loop forms. With the handshake (the reference's
+// loop, umma_2sm.cu:617-659, and the default of the umma_2sm CLI), every
+// iteration's commit arrives on both CTAs' mbarriers (two commits here, one
+// per CTA, where the reference sends one to both), each CTA waits on its own,
+// and all threads of both CTAs meet in a cluster barrier before the next
+// iteration, inside the timed region. Without it, only the issuing CTA waits
+// per iteration; the peer learns of the final MMA through one extra commit
+// after the loop, so the timed loop carries no cluster handshake.
 #include <atomic>
 
 #include "common.cuh"
@@ -39,7 +41,7 @@ template <int CG, int N, int DEPTH>
 __device__ __forceinline__ void probe_body(int64_t iterations, int timed, const uint16_t* __restrict__ a_g,
                                            const uint16_t* __restrict__ b_g, float* __restrict__ d_out,
                                            unsigned long long* __restrict__ cycles, int* __restrict__ launch_ok,
-                                           int* status) {
+                                           int* status, int handshake) {
   constexpr int kMLocal = 128;
   constexpr int kNLocal = N / CG;
   constexpr int kABytes = kMLocal * kK * 2;
@@ -91,7 +93,34 @@ __device__ __forceinline__ void probe_body(int64_t iterations, int timed, const 
   tc_fence_after();
   const uint32_t tmem_d = *reinterpret_cast<volatile uint32_t*>(&tmem_slot);
 
-  if (rank == 0 && tid == 0) {
+  const bool pair_handshake = CG == 2 && handshake != 0;
+  if (pair_handshake) {
+    // The reference's per-iteration handshake (see the header comment).
+    constexpr uint32_t idesc = make_idesc_bf16_f32(kMLocal * CG, N);
+    const uint64_t adesc = make_smem_desc(smem_u32(sa), 128, 256, kLayoutNone);
+    const uint64_t bdesc = make_smem_desc(smem_u32(sb), 128, 256, kLayoutNone);
+    const uint32_t mb = smem_u32(&mbar);
+    uint32_t parity = 0;
+    uint64_t c0 = 0;
+    if (rank == 0 && tid == 0) c0 = clock64_now();
+    for (int64_t it = 0; it < iterations; ++it) {
+      if (rank == 0 && tid == 0) {
+        umma_f16<CG>(tmem_d, adesc, bdesc, idesc, 0u);
+#pragma unroll
+        for (int d = 1; d < DEPTH; ++d) umma_f16<CG>(tmem_d, adesc, bdesc, idesc, 1u);
+        umma_commit<CG>(mb);
+        umma_commit<CG>(mapa_shared(mb, 1));
+      }
+      // Each CTA waits on its own barrier; after a timeout (status set) the
+      // remaining waits return at once, so the loop still ends.
+      if (tid == 0) bb_wait<true>(mb, parity, status, kDevTimeoutProbe, /*honor_abort=*/true);
+      parity ^= 1u;
+      __syncthreads();
+      cluster_sync();
+    }
+    if (rank == 0 && tid == 0 && timed) cycles[0] = static_cast<unsigned long long>(clock64_now() - c0);
+  }
+  if (!pair_handshake && rank == 0 && tid == 0) {
     constexpr uint32_t idesc = make_idesc_bf16_f32(kMLocal * CG, N);
     const uint64_t adesc = make_smem_desc(smem_u32(sa), 128, 256, kLayoutNone);
     const uint64_t bdesc = make_smem_desc(smem_u32(sb), 128, 256, kLayoutNone);
@@ -111,7 +140,7 @@ __device__ __forceinline__ void probe_body(int64_t iterations, int timed, const 
     if constexpr (CG == 2) umma_commit<CG>(mapa_shared(smem_u32(&peer_done), 1));
   }
   if constexpr (CG == 2) {
-    if (rank == 1 && tid == 0) {
+    if (!pair_handshake && rank == 1 && tid == 0) {
       bb_wait<true>(smem_u32(&peer_done), 0, status, kDevTimeoutProbe, /*honor_abort=*/false);
     }
   }
@@ -148,14 +177,14 @@ __device__ __forceinline__ void probe_body(int64_t iterations, int timed, const 
 #define BB_UMMA_1SM(N, D)                                                                                   \
   extern "C" __global__ void __launch_bounds__(128, 1) umma_1sm_m128n##N##k16_d##D(                         \
       int64_t iterations, int timed, const uint16_t* a, const uint16_t* b, float* d, unsigned long long* cyc, \
-      int* ok, int* st) {                                                                                   \
-    bb::umma::probe_body<1, N, D>(iterations, timed, a, b, d, cyc, ok, st);                                 \
+      int* ok, int* st, int hs) {                                                                           \
+    bb::umma::probe_body<1, N, D>(iterations, timed, a, b, d, cyc, ok, st, hs);                             \
   }
 #define BB_UMMA_2SM(N, D)                                                                                   \
   extern "C" __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1) umma_2sm_m256n##N##k16_d##D( \
       int64_t iterations, int timed, const uint16_t* a, const uint16_t* b, float* d, unsigned long long* cyc, \
-      int* ok, int* st) {                                                                                   \
-    bb::umma::probe_body<2, N, D>(iterations, timed, a, b, d, cyc, ok, st);                                 \
+      int* ok, int* st, int hs) {                                                                           \
+    bb::umma::probe_body<2, N, D>(iterations, timed, a, b, d, cyc, ok, st, hs);                             \
   }
 #define BB_UMMA_ALL_DEPTHS(M, N) M(N, 4) M(N, 16) M(N, 32) M(N, 64) M(N, 128) M(N, 256)
 BB_UMMA_ALL_DEPTHS(BB_UMMA_1SM, 64)
@@ -167,7 +196,8 @@ BB_UMMA_ALL_DEPTHS(BB_UMMA_2SM, 256)
 
 namespace {
 
-using ProbeFn = void (*)(int64_t, int, const uint16_t*, const uint16_t*, float*, unsigned long long*, int*, int*);
+using ProbeFn = void (*)(int64_t, int, const uint16_t*, const uint16_t*, float*, unsigned long long*, int*, int*,
+                         int);
 
 struct ProbeEntry {
   int cg, n, depth;
@@ -220,8 +250,9 @@ BB_API const char* bb_umma_kernel_name(int cta_group, int n, int depth) {
   return e ? e->name : nullptr;
 }
 
-BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int timed, const void* a, const void* b,
-                       float* d_out, unsigned long long* cycles, int* launch_ok, int* status, void* stream) {
+BB_API int bb_umma_run_ex(int cta_group, int n, int depth, int64_t iterations, int timed, int handshake,
+                          const void* a, const void* b, float* d_out, unsigned long long* cycles, int* launch_ok,
+                          int* status, void* stream) {
   using namespace bb;
   try {
     clear_error();
@@ -245,7 +276,7 @@ BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int 
     BB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     e->fn<<<cta_group, 128, smem, static_cast<cudaStream_t>(stream)>>>(
         iterations, timed, static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b), d_out, cycles,
-        launch_ok, status);
+        launch_ok, status, handshake);
     BB_CUDA_TRY(cudaGetLastError());
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return BB_OK;
@@ -253,6 +284,11 @@ BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int 
     bb::set_error("bb_umma_run: unexpected C++ exception");
     return BB_ERR_INTERNAL;
   }
+}
+
+BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int timed, const void* a, const void* b,
+                       float* d_out, unsigned long long* cycles, int* launch_ok, int* status, void* stream) {
+  return bb_umma_run_ex(cta_group, n, depth, iterations, timed, 0, a, b, d_out, cycles, launch_ok, status, stream);
 }
 
 BB_API int bb_test_wait_timeout(int64_t budget_ns, int* status, void* stream) {

@@ -34,14 +34,20 @@ def flops_per_umma(cta_group: int, n: int) -> int:
 
 
 class UmmaProbe:
-    def __init__(self, cta_group: int, n: int, depth: int, a: torch.Tensor, b: torch.Tensor, stream=None):
+    def __init__(self, cta_group: int, n: int, depth: int, a: torch.Tensor, b: torch.Tensor, stream=None,
+                 handshake: bool = False):
+        """handshake=True (CTA pairs only): the reference's per-iteration
+        cluster handshake inside the timed loop (umma_2sm.cu:617-659)."""
         if a.shape != (m_of(cta_group), K) or b.shape != (n, K):
             raise ValueError(f"operands must be A {(m_of(cta_group), K)} and B {(n, K)}")
         if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or not a.is_cuda or not b.is_cuda:
             raise ValueError("operands must be CUDA bfloat16 tensors")
         if a.device != b.device:
             raise ValueError(f"A on {a.device}, B on {b.device}: both must be on one device")
+        if handshake and cta_group != 2:
+            raise ValueError("the handshake loop is a CTA-pair (cta_group 2) form")
         self.cta_group, self.n, self.depth = cta_group, n, depth
+        self.handshake = bool(handshake)
         self.name = kernel_name(cta_group, n, depth)
         self.a, self.b = a.contiguous(), b.contiguous()
         dev = a.device
@@ -54,10 +60,10 @@ class UmmaProbe:
 
     def launch(self, iterations: int, timed: bool = True) -> None:
         self.launch_ok.zero_()
-        nat.check("bb_umma_run", self._lib.bb_umma_run(
-            self.cta_group, self.n, self.depth, iterations, 1 if timed else 0, self.a.data_ptr(), self.b.data_ptr(),
-            self.d.data_ptr(), self.cycles.data_ptr(), self.launch_ok.data_ptr(), self.status.data_ptr(),
-            self.stream.cuda_stream))
+        nat.check("bb_umma_run_ex", self._lib.bb_umma_run_ex(
+            self.cta_group, self.n, self.depth, iterations, 1 if timed else 0, 1 if self.handshake else 0,
+            self.a.data_ptr(), self.b.data_ptr(), self.d.data_ptr(), self.cycles.data_ptr(),
+            self.launch_ok.data_ptr(), self.status.data_ptr(), self.stream.cuda_stream))
 
     def result(self) -> tuple[torch.Tensor, int]:
         """(D on the host, elapsed cycles); raises on a launch or wait failure."""

@@ -223,6 +223,14 @@ BB_API int bb_fill_uniform_u32(void* dst, int64_t bytes, uint64_t seed, void* st
 BB_API int bb_umma_run(int cta_group, int n, int depth, int64_t iterations, int timed, const void* a,
                        const void* b, float* d_out, unsigned long long* cycles, int* launch_ok, int* status,
                        void* stream);
+/* bb_umma_run with the 2-SM loop form chosen: handshake != 0 (cta_group 2
+ * only) runs the reference's per-iteration handshake inside the timed loop
+ * (each commit arrives on both CTAs' mbarriers, each CTA waits on its own,
+ * then a cluster barrier of all threads: umma_2sm.cu:617-659); handshake = 0
+ * is bb_umma_run's loop (only the issuing CTA waits per iteration). */
+BB_API int bb_umma_run_ex(int cta_group, int n, int depth, int64_t iterations, int timed, int handshake,
+                          const void* a, const void* b, float* d_out, unsigned long long* cycles, int* launch_ok,
+                          int* status, void* stream);
 /* Kernel symbol name of one probe specialisation (e.g.
  * "umma_1sm_m128n256k16_d256"), or NULL. */
 BB_API const char* bb_umma_kernel_name(int cta_group, int n, int depth);

@@ -91,3 +91,23 @@ def test_tiny_buffers(cuda_device, method, row_bytes, nbytes):
         want = oracle.copy_checksums(words, run.info["stage_bytes"], run.info["grid_ctas"], 2)
         assert np.array_equal(got, want), (stages, run.info)
         run.check_status()
+
+
+@pytest.mark.parametrize("pipe", ["0", "1"])
+@pytest.mark.parametrize("stages,bif", [(2, 64), (4, 32), (8, 16)])
+def test_ldgsts_pipeline_forms_same_checksums(cuda_device, monkeypatch, pipe, stages, bif):
+    """Both LDGSTS pipeline forms (classic: reduce a landed tile, then issue
+    into the freed slot; refill: each position refilled right after it was
+    read; BB_COPY_PIPE) read the same words over several passes with
+    rotation, on a buffer whose last tile is short."""
+    monkeypatch.setenv("BB_COPY_PIPE", pipe)
+    nbytes = 9 * 1024 * 1024 + 512
+    buf = torch.empty(nbytes // 4, dtype=torch.int32, device=cuda_device)
+    streaming.fill_uniform_u32(buf, seed=3)
+    words = oracle.uniform_u32(nbytes // 4, seed=3)
+    run = streaming.StreamingRun("ldgsts", stages, bif, buf, row_bytes=256)
+    for passes, rotation in ((1, 0), (3, 2)):
+        run.run(passes=passes, rotation=rotation)
+        want = oracle.copy_checksums(words, run.info["stage_bytes"], run.info["grid_ctas"], passes)
+        assert np.array_equal(np.array(run.checksums(), dtype=np.uint32), want)
+    run.check_status()

@@ -10,12 +10,14 @@ from gb300_microbench_b200 import inputs, umma
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("cta_group", (1, 2))
+@pytest.mark.parametrize("cta_group,handshake", ((1, False), (2, False), (2, True)))
 @pytest.mark.parametrize("n", umma.N_VALUES)
 @pytest.mark.parametrize("depth", umma.ALL_DEPTHS)
-def test_pattern_exact(cuda_device, cta_group, n, depth):
+def test_pattern_exact(cuda_device, cta_group, handshake, n, depth):
+    """Both 2-SM loop forms (with the reference's per-iteration CTA-pair
+    handshake, and without) give the exact known answer."""
     a, b = inputs.umma_pattern_operands(cta_group, n)
-    probe = umma.UmmaProbe(cta_group, n, depth, a.to(cuda_device), b.to(cuda_device))
+    probe = umma.UmmaProbe(cta_group, n, depth, a.to(cuda_device), b.to(cuda_device), handshake=handshake)
     probe.launch(iterations=2, timed=True)
     d, cycles = probe.result()
     want = oracle.umma_reference_d(cta_group, n, depth)
