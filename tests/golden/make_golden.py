@@ -1,10 +1,10 @@
 """Regenerates the golden fixtures of tests/golden/ from the reference.
 
-Run in a container that has the reference tree (default /root/reference)
+Run in a container that has the reference tree (GB300_REFERENCE or --reference)
 and the CuTe DSL package the reference's driver uses:
 
-    make -C oracle ref REFERENCE=/root/reference
-    python tests/golden/make_golden.py [--reference /root/reference]
+    make -C oracle ref REFERENCE=$GB300_REFERENCE
+    python tests/golden/make_golden.py [--reference PATH]
 
 * gemm_reference_inputs.json: a small reference-mode operand draw made with
   the reference's own input helper, exactly as the pinned upstream
@@ -19,6 +19,7 @@ and the CuTe DSL package the reference's driver uses:
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -71,7 +72,7 @@ def write_csv_headers(reference: Path) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GB300_REFERENCE"), required=not os.environ.get("GB300_REFERENCE"))
     args = ap.parse_args()
 
     import torch

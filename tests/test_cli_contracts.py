@@ -7,6 +7,7 @@ Checks that need the reference tree skip where it is absent."""
 import csv
 import importlib.util
 import json
+import os
 import random
 import sys
 from pathlib import Path
@@ -19,10 +20,12 @@ from gb300_microbench_b200.cli import umma as um
 
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = Path(__file__).resolve().parent / "golden"
-REFERENCE = Path("/root/reference")
+REFERENCE = Path(os.environ["GB300_REFERENCE"]) if os.environ.get("GB300_REFERENCE") else None
 
 
 def _ref_module(rel: str, name: str):
+    if REFERENCE is None:
+        pytest.skip("GB300_REFERENCE does not name the reference tree")
     path = REFERENCE / rel
     if not path.exists():
         pytest.skip("reference tree not present")
