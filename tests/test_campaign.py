@@ -51,3 +51,35 @@ def test_useful_bytes_parsing():
 def test_bad_campaign_id_refused(argv, monkeypatch):
     monkeypatch.setenv("B200_GIT_COMMIT", "a" * 40)
     assert cp.main(argv) == 2
+
+
+def _ref_analyze():
+    ref = os.environ.get("GB300_REFERENCE")
+    if not ref or not Path(ref, "analysis", "analyze.py").exists():
+        pytest.skip("GB300_REFERENCE does not name the reference tree")
+    for sub in ("scripts", "analysis"):
+        sys.path.insert(0, str(Path(ref, sub)))
+    spec = importlib.util.spec_from_file_location("ref_analyze_campaigns", Path(ref, "analysis", "analyze.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+CAMPAIGNS = Path(__file__).resolve().parents[1] / "results" / "campaigns"
+
+
+def test_committed_campaigns_pass_reference_analysis():
+    """The three committed campaigns pass the reference's campaign reader
+    (manifest schema, artifact hashes, the row validators, the profile
+    index and hashes) and its population check, and its analysis derives the
+    counter-based figures from their profiles."""
+    an = _ref_analyze()
+    dirs = sorted(p for p in CAMPAIGNS.iterdir() if p.is_dir()) if CAMPAIGNS.exists() else []
+    if len(dirs) != 3:
+        pytest.skip("no committed campaigns")
+    records = [an.campaign(d) for d in dirs]
+    an.validate_population(records)
+    assert all(r["profiles"]["state"] in ("COMPLETE", "PARTIAL") for r in records)
+    _, mem = an.memory_analysis(records)
+    _, umma = an.umma_analysis(records)
+    assert len(mem["configurations"]) == 18 and len(umma["configurations"]) == 24
