@@ -3,6 +3,7 @@
 beside this build's kernel and cuBLASLt, on the same B200 (one GPU).
 
     python baseline/run_reference_gemm.py [--iterations N] [--warmup-iterations N] [--out results/...csv]
+        [--shapes 4096x4096x4096x1,...] [--variants persistent_2cta,...]
 
 The reference's gemm_comparison.py builds three candidates from the pinned
 CUTLASS examples ``blackwell/dense_gemm.py`` (DenseGemmKernel) and
@@ -82,7 +83,11 @@ def main(argv=None) -> int:
     ap.add_argument("--iterations", type=int, default=20)
     ap.add_argument("--warmup-iterations", type=int, default=5)
     ap.add_argument("--out", default=str(ROOT / "results" / "reference_on_b200_gemm.csv"))
+    ap.add_argument("--shapes", default="", help="comma-separated MxNxKxL subset of the five shapes")
+    ap.add_argument("--variants", default="", help="comma-separated subset of the slots (and ours' variants)")
     args = ap.parse_args(argv)
+    shapes = [s for s in SHAPES if not args.shapes or "x".join(map(str, s)) in args.shapes.split(",")]
+    keep = set(args.variants.split(",")) if args.variants else None
 
     import cuda.bindings.driver as cuda
     import cutlass
@@ -100,7 +105,7 @@ def main(argv=None) -> int:
     cute_stream = cuda.CUstream(torch_stream.cuda_stream)
     rows = []
     compiled = {}
-    for (m, n, k, l) in SHAPES:
+    for (m, n, k, l) in shapes:
         flops = 2.0 * m * n * k * l
         (a_t, b_t, c_t, a_cpu, b_cpu, _c_cpu, c_gpu) = modules[False].create_tensors(
             l, m, n, k, "k", "k", "n", cutlass.BFloat16, cutlass.Float32)
@@ -108,6 +113,8 @@ def main(argv=None) -> int:
         shape = f"{m}x{n}x{k}x{l}"
 
         for variant, cls_name, tiler, cluster, two_cta, persistent in SLOTS:
+            if keep is not None and variant not in keep:
+                continue
             gemm = getattr(modules[persistent], cls_name)(cutlass.Float32, two_cta, tiler, cluster, True)
             if persistent:
                 ok = gemm.can_implement((m, n, k, l), a_t.element_type, b_t.element_type, c_t.element_type,
@@ -145,6 +152,8 @@ def main(argv=None) -> int:
         b2 = b_cpu.permute(2, 0, 1).contiguous().cuda()  # (L, N, K)
         ref2 = ref.permute(2, 0, 1)
         for variant in VARIANTS:
+            if keep is not None and variant not in keep:
+                continue
             c2 = torch.full((l, m, n), float("nan"), dtype=torch.float32, device="cuda")
             plan = GemmPlan(a2, b2, c2, variant=variant)
             plan.run()

@@ -445,6 +445,13 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
         for (int ks = 0; ks < p.k_stages; ++ks) {
           uint32_t d_tmem = tmem_base + acc_col;
           uint32_t buf = 0;
+          // The stage's operands are normally resident long before its
+          // partial buffer is free (FP8), so the data wait comes first and
+          // only the buffer hand-off stands between the release and the MMAs.
+          if (!bb_wait_warp<kPair, !C::kSpinWaits>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
           if constexpr (kKind == kFp8Block) {
             buf = acc_iter % C::FP8_BUFS;
             if (!bb_wait_warp<kPair, !C::kSpinWaits>(smem_u32(&acc_empty[buf]), ((acc_iter / C::FP8_BUFS) & 1u) ^ 1u,
@@ -452,12 +459,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
               ok = false;
               break;
             }
-            tc_fence_after();
             d_tmem = tmem_base + buf * C::TILE_N;
-          }
-          if (!bb_wait_warp<kPair, !C::kSpinWaits>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
-            ok = false;
-            break;
           }
           tc_fence_after();
           if (elect_one()) {
@@ -607,10 +609,30 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
         float acc[C::WARP_COLS];
 #pragma unroll
         for (int j = 0; j < C::WARP_COLS; ++j) acc[j] = 0.f;
-        float s_next = __ldg(sa_row) * __ldg(sb_row);
+        // Lane l holds the scale product of K block w + l of the current
+        // 32-block window (s_win) and the raw scales of the next window,
+        // loaded a whole window ahead: the per-block loop reads its scale
+        // with one shuffle and never waits on a global load (a load issued
+        // one block ahead still stalled each block for an L2 round trip,
+        // right before the wait on the MMA hand-off).
+        float ra, rb;
+        auto load_raw = [&](int kk) {
+          ra = 0.f;
+          rb = 0.f;
+          if (kk < p.k_stages) {
+            ra = __ldg(sa_row + kk);
+            rb = __ldg(sb_row + kk);
+          }
+        };
+        load_raw(lane);
+        float s_win = ra * rb;
+        load_raw(32 + lane);
         for (int ks = 0; ks < p.k_stages; ++ks) {
-          const float s = s_next;
-          if (ks + 1 < p.k_stages) s_next = __ldg(sa_row + ks + 1) * __ldg(sb_row + ks + 1);
+          if ((ks & 31) == 0 && ks > 0) {
+            s_win = ra * rb;
+            load_raw(ks + 32 + lane);
+          }
+          const float s = __shfl_sync(0xffffffffu, s_win, ks & 31);
           const uint32_t buf = acc_iter % C::FP8_BUFS;
           // Spin without the suspend hint: this wait is on the per-K-block
           // MMA -> promotion -> MMA hand-off, where wake-up latency counts.
@@ -838,13 +860,15 @@ BB_API int bb_lowp_plan_create(int kind, int64_t m, int64_t n, int64_t k, const 
     h->n = n;
     h->k = k;
     h->stream = static_cast<cudaStream_t>(stream);
-    // NVFP4: CTA pairs (256-row tiles) unless A has a single 128-row block.
-    // FP8: single CTAs. Its epilogue promotes every 128-wide K block; that
-    // per-block chain (wait, TMEM loads, release, promotion) bounds both tile
-    // shapes alike (8192^3: 2160 single, 2210 pair TFLOP/s), and the single
-    // CTA has no cross-CTA hand-off.
-    // BB_LOWP_CTA_GROUP=1|2 forces one.
-    h->cg = (kind == BB_LOWP_NVFP4 && m > 128) ? 2 : 1;
+    // CTA pairs (256-row tiles) unless A has a single 128-row block. For
+    // FP8 the pair is the only shape that can approach the tensor rate: a
+    // single CTA's 128 x 256 tile moves 96 KiB of shared memory per 128-K
+    // block (48 KiB of TMA writes, 48 KiB of MMA operand reads) against the
+    // pair's 64 KiB, i.e. about 750 against 500 clocks at 128 B/clock for
+    // 512 clocks of MMA. The pair's price is its per-block accumulator
+    // hand-off across the CTAs (8192^3: pair 2320-2377, single 2200-2250
+    // TFLOP/s). BB_LOWP_CTA_GROUP=1|2 forces one.
+    h->cg = m > 128 ? 2 : 1;
     if (const char* env = std::getenv("BB_LOWP_CTA_GROUP")) {
       if (env[0] == '1') h->cg = 1;
       if (env[0] == '2') h->cg = 2;

@@ -32,6 +32,11 @@ enum : int {
 // Two seconds of wall time per individual wait. A healthy wait in any kernel
 // of this library lasts microseconds; a wait this long means a lost arrival.
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
+// A waiting thread reads the shared abort word (a global load) at most once
+// per kAbortPollNs of waiting. Every waiting warp of every CTA polls the same
+// word, so frequent reads keep one L2 slice busy with them, and that slice
+// also serves its share of the operand tiles the kernels stream.
+constexpr uint64_t kAbortPollNs = 20000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -197,15 +202,20 @@ __device__ __forceinline__ bool bb_wait(uint32_t addr, uint32_t parity, int* sta
   };
   if (probe()) return true;
   const uint64_t t0 = globaltimer_ns();
+  uint64_t next_abort_check = t0 + kAbortPollNs;
   uint32_t spins = 0;
   while (true) {
     if (probe()) return true;
     if ((++spins & 31u) == 0) {
-      if (globaltimer_ns() - t0 > budget_ns) {
+      const uint64_t now = globaltimer_ns();
+      if (now - t0 > budget_ns) {
         if (status) atomicCAS(status, 0, code);
         return false;
       }
-      if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) return false;
+      if (honor_abort && status && now >= next_abort_check) {
+        if (*reinterpret_cast<volatile int*>(status) != 0) return false;
+        next_abort_check = now + kAbortPollNs;
+      }
     }
   }
 }
@@ -233,6 +243,7 @@ __device__ __forceinline__ bool bb_wait_warp(uint32_t addr, uint32_t parity, int
     // The budget and the abort word (a global load) are checked every 8th
     // probe only: a phase that completes during those checks is seen late.
     const uint64_t t0 = globaltimer_ns();
+    uint64_t next_abort_check = t0 + kAbortPollNs;
     uint32_t spins = 0;
     while (true) {
       if (probe()) {
@@ -240,11 +251,15 @@ __device__ __forceinline__ bool bb_wait_warp(uint32_t addr, uint32_t parity, int
         break;
       }
       if ((++spins & 7u) == 0) {
-        if (globaltimer_ns() - t0 > budget_ns) {
+        const uint64_t now = globaltimer_ns();
+        if (now - t0 > budget_ns) {
           if (status && (threadIdx.x % 32) == 0) atomicCAS(status, 0, code);
           break;
         }
-        if (honor_abort && status && *reinterpret_cast<volatile int*>(status) != 0) break;
+        if (honor_abort && status && now >= next_abort_check) {
+          if (*reinterpret_cast<volatile int*>(status) != 0) break;
+          next_abort_check = now + kAbortPollNs;
+        }
       }
     }
   }
