@@ -136,8 +136,9 @@ def test_committed_result_csvs_pass_campaign_validators():
 def test_committed_result_csvs_feed_reference_analysis(tmp_path):
     """The reference's cross-campaign statistics (analysis/analyze.py:484-886)
     and figures (:1099) consume the committed B200 CSVs unchanged. The three
-    campaign records are the same CSVs three times (one campaign was run
-    here); counter-derived figures need ncu profiles and read as absent."""
+    records here are the same sweep CSVs three times, with no profiles; the
+    three measured campaigns with their Nsight Compute captures are checked
+    by tests/test_campaign.py."""
     an = _ref_module("analysis/analyze.py", "ref_analyze")
 
     def rows(name):
