@@ -486,8 +486,10 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
               for (int g = 0; g < C::MMAS; ++g)
                 mma_f8<kCG>(d_tmem, a_desc + 2 * g, b_desc + 2 * g, idesc, g != 0 ? 1u : 0u);
             }
+            // FP8: this commit also tells the epilogue that K block
+            // acc_iter's partial is complete (its wait is on the stage's
+            // barrier), so no second commit per block is needed.
             commit_both(&empty[stage]);
-            if constexpr (kKind == kFp8Block) commit_both(&acc_full[buf]);
           }
           __syncwarp();
           if constexpr (kKind == kFp8Block) ++acc_iter;
@@ -634,9 +636,15 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
           }
           const float s = __shfl_sync(0xffffffffu, s_win, ks & 31);
           const uint32_t buf = acc_iter % C::FP8_BUFS;
+          // K block acc_iter's partial is complete when the MMA's commit
+          // releases its operand stage (one stage per K block, stage =
+          // acc_iter % STAGES, that barrier's phase acc_iter / STAGES). The
+          // parity cannot be overtaken: the MMA can run at most FP8_BUFS
+          // blocks ahead of this wait, and STAGES > FP8_BUFS.
           // Spin without the suspend hint: this wait is on the per-K-block
           // MMA -> promotion -> MMA hand-off, where wake-up latency counts.
-          if (!bb_wait_warp<kPair, false>(smem_u32(&acc_full[buf]), (acc_iter / C::FP8_BUFS) & 1u, p.status,
+          static_assert(STAGES > C::FP8_BUFS, "stage barrier reused before the epilogue saw it");
+          if (!bb_wait_warp<kPair, false>(smem_u32(&empty[acc_iter % STAGES]), (acc_iter / STAGES) & 1u, p.status,
                                           kDevTimeoutEpilogue)) {
             ok = false;
             break;
