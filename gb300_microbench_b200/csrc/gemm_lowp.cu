@@ -54,6 +54,13 @@ enum Kind : int { kNvfp4 = BB_LOWP_NVFP4, kFp8Block = BB_LOWP_FP8_BLOCK128 };
 
 constexpr int BM = 128;         // accumulator rows per CTA
 constexpr int ROW_BYTES = 128;  // K bytes of one stage row (one 128-byte swizzle row)
+// Every ring and hand-off wait acquires at CTA scope, also for barriers the
+// peer CTA of a pair signals (its TMA completions, its commits, its relaxed
+// arrivals): what the waiter then touches is read by the tensor core
+// (operands, TMEM), whose ordering comes from the barrier's phase and the
+// tcgen05 fences, not from a cluster-scope acquire. A completed-phase wait
+// costs about 27 clocks at CTA scope against about 50 at cluster scope.
+constexpr bool kCtaScope = false;  // bb_wait_warp's kClusterScope argument
 constexpr int SF_ATOM = 512;    // bytes of one scale atom (128 rows x 4 scales)
 constexpr int EPI_WARPS = 8;
 constexpr int kLaunchRegs = 168;  // registers per thread the kernels are built for
@@ -364,7 +371,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
       const int b_row = n_blk * C::TILE_N + static_cast<int>(rank) * C::B_ROWS;
       const int sfa_blk = m_blk * kCG + static_cast<int>(rank);
       for (int ks = 0; ks < p.k_stages; ++ks) {
-        if (!bb_wait_warp<kPair>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
+        if (!bb_wait_warp<kCtaScope>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) {
           ok = false;
           break;
         }
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
       // Tail: wait until the MMA has released every stage, so no commit
       // arrival can still be in flight towards this CTA when it exits.
       for (int i = 0; i < STAGES; ++i) {
-        if (!bb_wait_warp<kPair>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
+        if (!bb_wait_warp<kCtaScope>(smem_u32(&empty[stage]), phase ^ 1u, p.status, kDevTimeoutProducer)) break;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -429,12 +436,12 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
           // Tile j goes to buffer j % 2: wait until tile j - 2 left it, and
           // until tile j - 1 (the other buffer) drained the shared subtile.
           const uint32_t b = acc_iter & 1u;
-          if (!bb_wait_warp<kPair>(smem_u32(&acc_empty[b]), ((acc_iter >> 1) & 1u) ^ 1u, p.status,
+          if (!bb_wait_warp<kCtaScope>(smem_u32(&acc_empty[b]), ((acc_iter >> 1) & 1u) ^ 1u, p.status,
                                    kDevTimeoutMma)) {
             ok = false;
             break;
           }
-          if (acc_iter > 0 && !bb_wait_warp<kPair>(smem_u32(&ovl_free[b ^ 1u]), ((acc_iter - 1) >> 1) & 1u,
+          if (acc_iter > 0 && !bb_wait_warp<kCtaScope>(smem_u32(&ovl_free[b ^ 1u]), ((acc_iter - 1) >> 1) & 1u,
                                                    p.status, kDevTimeoutMma)) {
             ok = false;
             break;
@@ -448,13 +455,13 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
           // The stage's operands are normally resident long before its
           // partial buffer is free (FP8), so the data wait comes first and
           // only the buffer hand-off stands between the release and the MMAs.
-          if (!bb_wait_warp<kPair, !C::kSpinWaits>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
+          if (!bb_wait_warp<kCtaScope, !C::kSpinWaits>(smem_u32(&full[stage]), phase, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           if constexpr (kKind == kFp8Block) {
             buf = acc_iter % C::FP8_BUFS;
-            if (!bb_wait_warp<kPair, !C::kSpinWaits>(smem_u32(&acc_empty[buf]), ((acc_iter / C::FP8_BUFS) & 1u) ^ 1u,
+            if (!bb_wait_warp<kCtaScope, !C::kSpinWaits>(smem_u32(&acc_empty[buf]), ((acc_iter / C::FP8_BUFS) & 1u) ^ 1u,
                                                      p.status, kDevTimeoutMma)) {
               ok = false;
               break;
@@ -570,7 +577,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
       uint32_t pk[C::WARP_COLS / 2];
       if constexpr (kKind == kNvfp4) {
         const uint32_t b = acc_iter & 1u;
-        if (!bb_wait_warp<kPair>(smem_u32(&acc_full[b]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) break;
+        if (!bb_wait_warp<kCtaScope>(smem_u32(&acc_full[b]), (acc_iter >> 1) & 1u, p.status, kDevTimeoutEpilogue)) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_off + b * kAccStride + half * C::WARP_COLS;
         // The subtile shared with the other buffer is columns [192, 256) of
@@ -644,7 +651,7 @@ __global__ void __launch_bounds__(Cfg<kKind, kCG>::THREADS, 1)
           // Spin without the suspend hint: this wait is on the per-K-block
           // MMA -> promotion -> MMA hand-off, where wake-up latency counts.
           static_assert(STAGES > C::FP8_BUFS, "stage barrier reused before the epilogue saw it");
-          if (!bb_wait_warp<kPair, false>(smem_u32(&empty[acc_iter % STAGES]), (acc_iter / STAGES) & 1u, p.status,
+          if (!bb_wait_warp<kCtaScope, false>(smem_u32(&empty[acc_iter % STAGES]), (acc_iter / STAGES) & 1u, p.status,
                                           kDevTimeoutEpilogue)) {
             ok = false;
             break;
