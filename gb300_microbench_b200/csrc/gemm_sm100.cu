@@ -233,6 +233,7 @@ struct Cfg {
   static_assert(B_BYTES % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle atoms need 1 KiB alignment");
   // MMA shape legality for kind::f16: M=128 needs N%16==0, 16<=N<=256;
   // M=256 (cta_group::2) the same.
+  static_assert(N_SUB == 1 || N_SUB == 2, "the MMA loop issues one or two N = 256 halves per K step");
   static_assert(MMA_N % 16 == 0 && MMA_N >= 16 && MMA_N <= 256 && kBN % MMA_N == 0, "UMMA N");
 };
 
@@ -432,10 +433,14 @@ __global__ void __launch_bounds__(Cfg<kCG, kBN, kOutF32>::THREADS, 1)
             const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * (C::B_BYTES >> 4);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
-#pragma unroll
-              for (int h = 0; h < C::N_SUB; ++h) {
-                umma_f16<kCG>(d_tmem + h * C::MMA_N, a_desc + 2 * kk, b_desc + h * (C::B_SUB_BYTES >> 4) + 2 * kk,
-                              idesc, (kb != it.kb0 || kk != 0) ? 1u : 0u);
+              const uint32_t acc_in = (kb != it.kb0 || kk != 0) ? 1u : 0u;
+              if constexpr (C::N_SUB == 2) {
+                // Both N = 256 halves use this K step's A: read it once.
+                umma_f16_keep_a<kCG, true>(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, acc_in);
+                umma_f16_keep_a<kCG, false>(d_tmem + C::MMA_N, a_desc + 2 * kk,
+                                            b_desc + (C::B_SUB_BYTES >> 4) + 2 * kk, idesc, acc_in);
+              } else {
+                umma_f16<kCG>(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, acc_in);
               }
             }
             const uint32_t eb = smem_u32(&empty[stage]);
